@@ -1,0 +1,178 @@
+/*
+ * qlinear.h -- C ABI of the B200 (sm_100a) quantized-linear library.
+ *
+ * Drop-in replacement for the subset of the rk_npu_* C ABI that open_rknpu2_lm_infer's
+ * quantized-linear backend binds through bindgen (build.rs:49-68, allowlist rk_npu_.*)
+ * and calls from src/npu.rs.  The mapping, function by function, is given beside each
+ * declaration as "replaces <reference call> (file:line)".
+ *
+ * Path: dynamic per-token symmetric int8 activation quantisation -> W4/W8 x int8
+ * GEMM/GEMV with exact int32 accumulation -> (f32(acc) * s_a) * s_w epilogue, written as
+ * f32 (host API, bit-exact with the reference's CPU oracle src/npu.rs:1097-1121) or fp16
+ * (device API, the same f32 value rounded once to nearest-even).
+ *
+ * Conventions (mirroring the reference's):
+ *   - object handles are opaque; *_create returns NULL on failure (src/npu.rs:123-131)
+ *     and qlinear_last_status() then gives the reason;
+ *   - every other call returns an int status, 0 = QLINEAR_OK; qlinear_strerror()
+ *     gives its text (src/npu.rs:138-144);
+ *   - weight codes are passed in the reference's QuantMatrix layout: int8 [K][N]
+ *     row-major, element (k, n) at codes[k*N + n] (src/npu.rs:112-118, :1115), W4 codes
+ *     in [-8, 7] one per byte, W8 codes in [-127, 127]; scales f32 [N], > 0;
+ *   - a backend and everything created from it are used from one host thread at a time
+ *     (the reference's Backend is Rc<RefCell<..>>, src/npu.rs:252-254);
+ *   - nothing aborts or traps; device-side waits are bounded and report
+ *     QLINEAR_ERR_TIMEOUT.
+ *
+ * No symbol here uses torch or CUDA runtime types: streams are passed as void*
+ * (a cudaStream_t), device buffers as plain pointers.
+ */
+#ifndef QLINEAR_H
+#define QLINEAR_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define QLINEAR_API __attribute__((visibility("default")))
+#else
+#define QLINEAR_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (replace RK_NPU_ERR_*, src/npu.rs:138-151) ---------------------- */
+#define QLINEAR_OK 0
+#define QLINEAR_ERR_PARAM (-1)       /* invalid argument or shape (RK_NPU_ERR_PARAM) */
+#define QLINEAR_ERR_ALLOC (-2)       /* device or pinned allocation failed */
+#define QLINEAR_ERR_CUDA (-3)        /* a CUDA runtime/driver call failed */
+#define QLINEAR_ERR_UNSUPPORTED (-4) /* valid request this build does not implement */
+#define QLINEAR_ERR_TIMEOUT (-5)     /* a bounded device-side wait gave up */
+#define QLINEAR_ERR_NCCL (-6)        /* an NCCL call failed */
+#define QLINEAR_ERR_STATE (-7)       /* object used in the wrong state */
+
+/* ---- rounding of the activation quantiser ------------------------------------------ */
+#define QLINEAR_ROUND_AWAY 0 /* f32::round, ties away from zero: the reference (src/npu.rs:1109) */
+#define QLINEAR_ROUND_EVEN 1 /* round half to even (opt-in; not the reference's) */
+
+/* ---- element types of device buffers ----------------------------------------------- */
+#define QLINEAR_F32 0
+#define QLINEAR_F16 1
+#define QLINEAR_I32 2 /* output only: raw int32 accumulators (parity export) */
+
+/* ---- run flags ----------------------------------------------------------------------- */
+#define QLINEAR_RUN_SWIGLU 1u /* out[m][j] = silu(y[m][j]) * y[m][N/2 + j], width N/2 */
+
+typedef struct qlinear_backend qlinear_backend;
+typedef struct qlinear_weights qlinear_weights;
+
+typedef struct qlinear_backend_config {
+    int device;     /* CUDA device ordinal (replaces the IOMMU domain id, src/npu.rs:310) */
+    int round_mode; /* QLINEAR_ROUND_AWAY (default) or QLINEAR_ROUND_EVEN */
+    int max_rows;   /* rows one host call may stage without reallocating; 0 = 256 */
+    int reserved;
+} qlinear_backend_config;
+
+typedef struct qlinear_weight_config {
+    int bits; /* 4 or 8 */
+    int K;    /* input features  (> 0) */
+    int N;    /* output features (> 0) */
+    int reserved;
+} qlinear_weight_config;
+
+typedef struct qlinear_weight_info {
+    int bits, K, N;
+    int K_padded;          /* K rounded up to the GEMM's 128-element k-block */
+    int N_padded;          /* N rounded up to the 128-channel tile */
+    uint64_t device_bytes; /* bytes of device memory the packed weights and scales hold */
+} qlinear_weight_info;
+
+/* Fills cfg with defaults (device 0, ties-away, 256 rows). */
+QLINEAR_API void qlinear_backend_config_init(qlinear_backend_config *cfg);
+
+/* Replaces rk_npu_open + rk_npu_iommu_domain_create (src/npu.rs:310-366). */
+QLINEAR_API qlinear_backend *qlinear_backend_create(const qlinear_backend_config *cfg);
+/* Replaces rk_npu_iommu_domain_free + rk_npu_close (Handle drop, src/npu.rs:133-137). */
+QLINEAR_API void qlinear_backend_free(qlinear_backend *backend);
+
+/* Replaces rk_npu_w4a8_weights_create (src/npu.rs:395-402) for bits == 4 and
+ * rk_npu_f32i8f32_weights_create (src/npu.rs:438-445) for bits == 8: copies codes
+ * [K][N] and scales [N] (host memory) into the device layout. */
+QLINEAR_API qlinear_weights *qlinear_weights_create(qlinear_backend *backend, const qlinear_weight_config *cfg,
+                                        const int8_t *codes_kn, const float *scales);
+/* Same, keeping only output columns [n_begin, n_end) of the matrix: the column-parallel
+ * (split-N) shard of one rank.  No reference counterpart (the reference is single-device). */
+QLINEAR_API qlinear_weights *qlinear_weights_create_shard(qlinear_backend *backend,
+                                              const qlinear_weight_config *cfg,
+                                              const int8_t *codes_kn, const float *scales,
+                                              int n_begin, int n_end);
+/* Same, from the checkpoint's compressed-tensors storage without the [K][N] transpose:
+ * bits == 4: weight_packed int32 [N][ceil(K/8)], nibble j of word w is k = 8w + j,
+ * stored as code + 8 (src/model/checkpoint.rs:352-371); bits == 8: weight int8 [N][K]
+ * (src/model/checkpoint.rs:372-378). */
+QLINEAR_API qlinear_weights *qlinear_weights_create_checkpoint(qlinear_backend *backend,
+                                                   const qlinear_weight_config *cfg,
+                                                   const void *storage, const float *scales);
+/* Replaces rk_npu_w4a8_weights_query / rk_npu_i4_weights_memory_query /
+ * rk_npu_f32i8f32_weights_memory_query (src/npu.rs:404-426, :447-453). */
+QLINEAR_API int qlinear_weights_query(const qlinear_weights *weights, qlinear_weight_info *info);
+/* Replaces rk_npu_w4a8_weights_free / rk_npu_f32i8f32_weights_free. */
+QLINEAR_API void qlinear_weights_free(qlinear_weights *weights);
+
+/* Replaces the workspace creation of Backend::prepare/get_work (src/npu.rs:595-615,
+ * :941-996): makes the per-call workspaces large enough for `rows` rows of every K/N
+ * loaded so far.  Optional: run calls grow the workspace on demand. */
+QLINEAR_API int qlinear_backend_prepare(qlinear_backend *backend, int rows);
+
+/* Replaces rk_npu_w4a8_run_f32 (src/npu.rs:1047) and rk_npu_f32i8f32_run_dynamic
+ * (src/npu.rs:1054): a_host f32 [rows][K] -> c_host f32 [rows][N], synchronous.
+ * Unlike the reference (rows <= 256, src/npu.rs:152-156) any rows >= 1 is accepted. */
+QLINEAR_API int qlinear_run_f32(qlinear_backend *backend, const qlinear_weights *weights, const float *a_host,
+                    float *c_host, int rows);
+/* Replaces rk_npu_w4a8_run_swiglu_f32 (src/npu.rs:1045): c_host f32 [rows][N/2] with
+ * c[m][j] = silu(y[m][j]) * y[m][N/2 + j].  N must be even.  Works for W4 and W8. */
+QLINEAR_API int qlinear_run_swiglu_f32(qlinear_backend *backend, const qlinear_weights *weights,
+                           const float *a_host, float *c_host, int rows);
+
+/* Device-resident path (no reference counterpart; the benchmark and multi-GPU path):
+ * a_dev [rows][K] of a_type (QLINEAR_F16 or QLINEAR_F32), c_dev [rows][ldc] of c_type
+ * (QLINEAR_F16, QLINEAR_F32 or QLINEAR_I32 raw accumulators), ldc >= output width
+ * (N, or N/2 with QLINEAR_RUN_SWIGLU).  Asynchronous on `stream` (a cudaStream_t; NULL =
+ * the legacy default stream).  Uses the backend's device workspace, so calls on one
+ * backend must be ordered on one stream. */
+QLINEAR_API int qlinear_run_device(qlinear_backend *backend, const qlinear_weights *weights,
+                       const void *a_dev, int a_type, void *c_dev, int c_type, long long ldc,
+                       int rows, unsigned flags, void *stream);
+
+/* Activation quantisation alone (parity export of the int8 codes): a_dev [rows][K] ->
+ * codes_dev int8 [rows][K], scales_dev f32 [rows], rowsums_dev int32 [rows] (may be NULL;
+ * sum of the row's codes).  Asynchronous on `stream`. */
+QLINEAR_API int qlinear_act_quant_device(qlinear_backend *backend, const void *a_dev, int a_type, int rows,
+                             int K, int8_t *codes_dev, float *scales_dev, int32_t *rowsums_dev,
+                             void *stream);
+
+/* Reads and clears the backend's device error word (bounded waits that gave up);
+ * synchronizes `stream` first.  Returns QLINEAR_OK or QLINEAR_ERR_TIMEOUT. */
+QLINEAR_API int qlinear_backend_check(qlinear_backend *backend, void *stream);
+
+/* Replaces Backend::stats (src/npu.rs:631-661): JSON text into buf (NUL-terminated).
+ * Returns the length needed (excluding NUL) or a negative status. */
+QLINEAR_API int qlinear_backend_stats(const qlinear_backend *backend, char *buf, size_t len);
+
+/* Number of kernels this backend has launched since creation (instrumentation). */
+QLINEAR_API unsigned long long qlinear_backend_launches(const qlinear_backend *backend);
+
+/* Replaces rk_npu_strerror (src/npu.rs:138-144). */
+QLINEAR_API const char *qlinear_strerror(int status);
+/* Status of the last failed *_create on this thread. */
+QLINEAR_API int qlinear_last_status(void);
+/* Library version string. */
+QLINEAR_API const char *qlinear_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QLINEAR_H */

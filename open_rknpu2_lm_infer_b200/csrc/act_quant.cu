@@ -1,0 +1,233 @@
+// act_quant.cu -- dynamic per-token symmetric int8 activation quantisation.
+//
+// Restates, per row m of x [rows][K] (f32 or fp16 widened exactly to f32), the
+// reference's quantiser (src/npu.rs:1099-1110, rk_npu_w4a8_quant in the un-vendored
+// operator library):
+//   amax  = max_k |x|          fmaxf ignores NaN like Rust's f32::max
+//   scale = amax == 0 ? 1 : max(amax / 127, FLT_MIN)       IEEE division
+//   inv   = 1 / scale                                        IEEE division
+//   q     = clamp(round(x * inv), -127, 127)                 roundf: ties away from zero
+//                                                            (rintf with QLINEAR_ROUND_EVEN)
+//   NaN -> 0 (Rust `NaN as i32`), +-inf -> +-127.
+// Writes int8 codes into a [rows][Kp] buffer (Kp = K rounded up to the 128-element
+// k-block, the pad zeroed), the f32 scale per row and the i32 sum of the row's codes
+// (used by the W4 epilogue, whose weights are stored offset by +8).
+//
+// One CTA per row; the row is read once with 16-byte loads and held in registers (up to
+// kCache chunks per thread; longer rows are re-read from L1/L2), the max is reduced with
+// warp shuffles (max is order independent, so the result is exact), codes are written
+// with 8-byte (fp16 input) or 4-byte (f32 input) stores.  HBM-bound: 2 or 4 bytes read
+// and 1 byte written per element.
+#include "common.cuh"
+#include "kernels.h"
+
+#include <float.h>
+
+namespace ql {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kCache = 6;
+
+template <typename T>
+struct Vec;
+template <>
+struct Vec<__half> {
+    static constexpr int N = 8;
+    __device__ static __forceinline__ void load(const __half *p, float (&v)[8]) {
+        uint4 raw = *reinterpret_cast<const uint4 *>(p);
+        const __half2 *h = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            float2 f = __half22float2(h[i]);
+            v[2 * i] = f.x;
+            v[2 * i + 1] = f.y;
+        }
+    }
+};
+template <>
+struct Vec<float> {
+    static constexpr int N = 4;
+    __device__ static __forceinline__ void load(const float *p, float (&v)[4]) {
+        float4 raw = *reinterpret_cast<const float4 *>(p);
+        v[0] = raw.x; v[1] = raw.y; v[2] = raw.z; v[3] = raw.w;
+    }
+};
+
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+
+__device__ __forceinline__ int quant_code(float v, float inv, int round_mode) {
+    float s = __fmul_rn(v, inv);
+    float r = round_mode ? rintf(s) : roundf(s);
+    int q = (r != r) ? 0 : __float2int_rz(r);
+    return max(-127, min(127, q));
+}
+
+__device__ __forceinline__ float block_max(float v, float *red) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    if (w == 0) {
+        v = l < (int)(blockDim.x >> 5) ? red[l] : 0.0f;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (l == 0) red[0] = v;
+    }
+    __syncthreads();
+    return red[0];
+}
+
+__device__ __forceinline__ int block_sum(int v, int *red) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    if (w == 0) {
+        v = l < (int)(blockDim.x >> 5) ? red[l] : 0;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (l == 0) red[0] = v;
+    }
+    __syncthreads();
+    return red[0];
+}
+
+__device__ __forceinline__ void row_scale(float amax, float &scale, float &inv) {
+    scale = amax == 0.0f ? 1.0f : fmaxf(__fdiv_rn(amax, 127.0f), FLT_MIN);
+    inv = __fdiv_rn(1.0f, scale);
+}
+
+// Vectorised path: K % VEC == 0 and every row 16-byte aligned.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) act_quant_vec_kernel(
+    const T *__restrict__ x, long long ldx, int K, int Kp, int round_mode,
+    int8_t *__restrict__ codes, float *__restrict__ scales, int32_t *__restrict__ rowsums) {
+    constexpr int V = Vec<T>::N;
+    __shared__ float redf[32];
+    __shared__ int redi[32];
+    const long long m = blockIdx.x;
+    const T *xr = x + m * ldx;
+    int8_t *cr = codes + m * (long long)Kp;
+    const int nchunks = K / V;
+
+    float v[kCache][V];
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kCache; i++) {
+        const int c = threadIdx.x + i * kThreads;
+        if (c < nchunks) {
+            Vec<T>::load(xr + (long long)c * V, v[i]);
+#pragma unroll
+            for (int e = 0; e < V; e++) amax = fmaxf(amax, fabsf(v[i][e]));
+        }
+    }
+    for (int c = threadIdx.x + kCache * kThreads; c < nchunks; c += kThreads) {
+        float t[V];
+        Vec<T>::load(xr + (long long)c * V, t);
+#pragma unroll
+        for (int e = 0; e < V; e++) amax = fmaxf(amax, fabsf(t[e]));
+    }
+    amax = block_max(amax, redf);
+    float scale, inv;
+    row_scale(amax, scale, inv);
+
+    int sum = 0;
+    auto emit = [&](int c, const float(&t)[V]) {
+        uint32_t w[V / 4];
+#pragma unroll
+        for (int g = 0; g < V / 4; g++) {
+            uint32_t packed = 0;
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int q = quant_code(t[4 * g + e], inv, round_mode);
+                sum += q;
+                packed |= (uint32_t)(q & 0xff) << (8 * e);
+            }
+            w[g] = packed;
+        }
+        if constexpr (V == 8)
+            *reinterpret_cast<uint2 *>(cr + (long long)c * 8) = make_uint2(w[0], w[1]);
+        else
+            *reinterpret_cast<uint32_t *>(cr + (long long)c * 4) = w[0];
+    };
+#pragma unroll
+    for (int i = 0; i < kCache; i++) {
+        const int c = threadIdx.x + i * kThreads;
+        if (c < nchunks) emit(c, v[i]);
+    }
+    for (int c = threadIdx.x + kCache * kThreads; c < nchunks; c += kThreads) {
+        float t[V];
+        Vec<T>::load(xr + (long long)c * V, t);
+        emit(c, t);
+    }
+    for (int k = K + threadIdx.x; k < Kp; k += kThreads) cr[k] = 0;
+    sum = block_sum(sum, redi);
+    if (threadIdx.x == 0) {
+        scales[m] = scale;
+        if (rowsums) rowsums[m] = sum;
+    }
+}
+
+// Scalar path for any K / alignment (re-reads the row for the second pass).
+template <typename T>
+__global__ void __launch_bounds__(kThreads) act_quant_scalar_kernel(
+    const T *__restrict__ x, long long ldx, int K, int Kp, int round_mode,
+    int8_t *__restrict__ codes, float *__restrict__ scales, int32_t *__restrict__ rowsums) {
+    __shared__ float redf[32];
+    __shared__ int redi[32];
+    const long long m = blockIdx.x;
+    const T *xr = x + m * ldx;
+    int8_t *cr = codes + m * (long long)Kp;
+    float amax = 0.0f;
+    for (int k = threadIdx.x; k < K; k += kThreads) amax = fmaxf(amax, fabsf(to_f32(xr[k])));
+    amax = block_max(amax, redf);
+    float scale, inv;
+    row_scale(amax, scale, inv);
+    int sum = 0;
+    for (int k = threadIdx.x; k < K; k += kThreads) {
+        const int q = quant_code(to_f32(xr[k]), inv, round_mode);
+        sum += q;
+        cr[k] = (int8_t)q;
+    }
+    for (int k = K + threadIdx.x; k < Kp; k += kThreads) cr[k] = 0;
+    sum = block_sum(sum, redi);
+    if (threadIdx.x == 0) {
+        scales[m] = scale;
+        if (rowsums) rowsums[m] = sum;
+    }
+}
+
+template <typename T>
+cudaError_t launch_typed(const T *x, long long ldx, int rows, int K, int Kp, int round_mode,
+                         int8_t *codes, float *scales, int32_t *rowsums, cudaStream_t stream) {
+    constexpr int V = Vec<T>::N;
+    const bool vec = (K % V == 0) && (ldx % V == 0) &&
+                     ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+    if (vec)
+        act_quant_vec_kernel<T><<<rows, kThreads, 0, stream>>>(x, ldx, K, Kp, round_mode, codes,
+                                                               scales, rowsums);
+    else
+        act_quant_scalar_kernel<T><<<rows, kThreads, 0, stream>>>(x, ldx, K, Kp, round_mode,
+                                                                  codes, scales, rowsums);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_act_quant(const void *x, int x_type, long long ldx, int rows, int K, int Kp,
+                             int round_mode, int8_t *codes, float *scales, int32_t *rowsums,
+                             cudaStream_t stream) {
+    if (rows <= 0) return cudaSuccess;
+    if (x_type == kF16)
+        return launch_typed(static_cast<const __half *>(x), ldx, rows, K, Kp, round_mode, codes,
+                            scales, rowsums, stream);
+    return launch_typed(static_cast<const float *>(x), ldx, rows, K, Kp, round_mode, codes, scales,
+                        rowsums, stream);
+}
+
+}  // namespace ql

@@ -1,0 +1,69 @@
+// kernels.h -- host-side launchers of the library's kernels (internal; not the C ABI).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ql {
+
+enum ElemType { kF32 = 0, kF16 = 1, kI32 = 2 };
+
+// Device weight layout (see pack.cu):
+//   W8: int8 [Np][Kp], row n holds codes w[k][n] for k < K, zero padding.
+//   W4: uint8 [Np][Kp/2]; each 4-byte word w of row n covers k = 8w .. 8w+7 and its
+//       byte j holds u(8w+j) | u(8w+j+4) << 4 with u = code + 8 (padding: code 0).
+struct WeightView {
+    int bits, K, N, Kp, Np;
+    const uint8_t *w;      // device
+    const float *scales;   // device, [Np], zero padded
+};
+
+// Activation workspace: codes int8 [rows_cap][Kp], scales f32 [rows_cap], rowsums i32.
+struct ActView {
+    const int8_t *codes;
+    const float *scales;
+    const int32_t *rowsums;
+    int rows_cap;          // rows the codes buffer holds (>= rows of the call)
+};
+
+cudaError_t launch_act_quant(const void *x, int x_type, long long ldx, int rows, int K, int Kp,
+                             int round_mode, int8_t *codes, float *scales, int32_t *rowsums,
+                             cudaStream_t stream);
+
+// Weight packing from the QuantMatrix layout int8 [K][N] (device copy) into the device
+// layout above; only columns [n_begin, n_begin + N) of a matrix with n_total columns.
+cudaError_t launch_pack_from_kn(const int8_t *codes_kn, int K, int n_total, int n_begin,
+                                const WeightView &w, uint8_t *dst, cudaStream_t stream);
+// From the checkpoint storage (W4: int32 words [N][ceil(K/8)], W8: int8 [N][K]).
+cudaError_t launch_pack_from_checkpoint(const void *storage, const WeightView &w, uint8_t *dst,
+                                        cudaStream_t stream);
+
+// Decode GEMV (rows <= 8).  out [rows][ldc] of out_type; swiglu: width N/2.
+cudaError_t launch_gemv(const WeightView &w, const ActView &a, int rows, void *out, int out_type,
+                        long long ldc, bool swiglu, int num_sms, cudaStream_t stream);
+
+// tcgen05 GEMM (any rows).  wmap / amap are the TMA descriptors of the weights and the
+// activation codes (see encode_* below).  out [rows][ldc] of out_type.
+struct GemmPlan {
+    int tok;        // token tile (the MMA's N): multiple of 16, <= 256
+    int stages;     // pipeline depth
+    int smem_bytes; // dynamic shared memory
+    int grid;       // persistent CTAs
+    int tiles;
+};
+GemmPlan plan_gemm(const WeightView &w, int rows, int num_sms);
+cudaError_t launch_gemm(const WeightView &w, const CUtensorMap &wmap, const ActView &a,
+                        const CUtensorMap &amap, const GemmPlan &plan, int rows, void *out,
+                        int out_type, long long ldc, unsigned *err, cudaStream_t stream);
+
+// SwiGLU over an f32 [rows][N] buffer: out[m][j] = silu(y[m][j]) * y[m][N/2 + j].
+cudaError_t launch_swiglu(const float *y, int rows, int N, void *out, int out_type,
+                          long long ldc, cudaStream_t stream);
+
+// TMA descriptor encoding through the driver entry point (no -lcuda link needed).
+bool tma_available();
+bool encode_weight_map(const WeightView &w, CUtensorMap *map);
+bool encode_act_map(const int8_t *codes, int rows_cap, int Kp, int tok, CUtensorMap *map);
+
+}  // namespace ql

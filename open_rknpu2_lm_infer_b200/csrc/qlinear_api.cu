@@ -1,0 +1,575 @@
+// qlinear_api.cu -- the C ABI of include/qlinear.h: backend and weight objects, workspace
+// management, dispatch between the decode GEMV (rows <= 8) and the tcgen05 GEMM, and the
+// synchronous host-f32 path that replaces the reference's rk_npu_*_run calls.
+//
+// Reference behaviour kept (src/npu.rs):
+//   - Backend::load validates bits (4|8), K/N > 0 and the code/scale lengths (:368-384);
+//   - Linear::run takes f32 rows [rows][K] and returns f32 [rows][N], synchronously
+//     (:1006, :1025-1071); Linear::run_swiglu returns [rows][N/2] (:1009-1024);
+//   - errors are int status codes with a message (:138-144), never an abort.
+// Deliberately different: no 256-row cap and no M-bucket padding (the GPU kernels mask
+// ragged tiles), no tuning (one static dispatch), run_swiglu supported for W4 and W8.
+#include "../../include/qlinear.h"
+#include "common.cuh"
+#include "kernels.h"
+
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <new>
+#include <string>
+#include <tuple>
+
+using namespace ql;
+
+struct qlinear_backend {
+    int device = 0;
+    int round_mode = QLINEAR_ROUND_AWAY;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;  // host-path calls and uploads
+    unsigned *d_err = nullptr;
+    unsigned *h_err = nullptr;      // pinned
+    // activation workspace
+    uint8_t *d_ws = nullptr;        // codes
+    size_t ws_bytes = 0;
+    float *d_ascale = nullptr;
+    int32_t *d_rowsum = nullptr;
+    size_t ws_rows = 0;
+    // f32 gate/up scratch for SwiGLU through the GEMM
+    float *d_y = nullptr;
+    size_t y_elems = 0;
+    // host path staging
+    void *d_in = nullptr, *d_out = nullptr;
+    size_t d_in_bytes = 0, d_out_bytes = 0;
+    void *h_in = nullptr, *h_out = nullptr;
+    size_t h_in_bytes = 0, h_out_bytes = 0;
+    // bookkeeping (Backend::stats)
+    int loaded_w4 = 0, loaded_w8 = 0;
+    uint64_t weight_bytes = 0;
+    int max_kp = 0, max_n = 0;
+    int prepared_rows = 0;
+    unsigned long long launches = 0;
+    unsigned long long gemv_calls = 0, gemm_calls = 0;
+    std::map<std::tuple<const void *, int, int, size_t>, CUtensorMap> amaps;
+};
+
+struct qlinear_weights {
+    qlinear_backend *backend = nullptr;
+    WeightView view{};
+    uint8_t *d_w = nullptr;
+    float *d_s = nullptr;
+    uint64_t bytes = 0;
+    CUtensorMap wmap{};
+};
+
+namespace {
+
+thread_local int g_last_status = QLINEAR_OK;
+
+// K * 127 * 127 must fit in int32 for the exact accumulator (W8; W4 is far looser).
+constexpr long long kMaxK = 133143;
+
+int fail(int status) {
+    g_last_status = status;
+    return status;
+}
+
+int cuda_status(cudaError_t e) {
+    if (e == cudaSuccess) return QLINEAR_OK;
+    if (e == cudaErrorMemoryAllocation) return QLINEAR_ERR_ALLOC;
+    return QLINEAR_ERR_CUDA;
+}
+
+#define QL_TRY(expr)                              \
+    do {                                          \
+        cudaError_t _e = (expr);                  \
+        if (_e != cudaSuccess) return cuda_status(_e); \
+    } while (0)
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+// ---------------------------------------------------------------- TMA descriptors
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+void load_encode() {
+    std::call_once(g_encode_once, [] {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+}
+
+bool encode_2d(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer,
+               uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+               CUtensorMapSwizzle swz) {
+    load_encode();
+    if (!g_encode) return false;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims,
+                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+namespace ql {
+bool tma_available() {
+    load_encode();
+    return g_encode != nullptr;
+}
+bool encode_weight_map(const WeightView &w, CUtensorMap *map) {
+    if (w.bits == 8)
+        return encode_2d(map, w.w, w.Kp, w.Np, w.Kp, KBLK, CH_TILE, CU_TENSOR_MAP_SWIZZLE_128B);
+    return encode_2d(map, w.w, w.Kp / 2, w.Np, w.Kp / 2, KBLK / 2, CH_TILE,
+                     CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+bool encode_act_map(const int8_t *codes, int rows_cap, int Kp, int tok, CUtensorMap *map) {
+    return encode_2d(map, codes, Kp, rows_cap, Kp, KBLK, tok, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+}  // namespace ql
+
+namespace {
+
+// ---------------------------------------------------------------- workspaces
+int ensure_act_ws(qlinear_backend *b, int rows, int Kp) {
+    const size_t need = (size_t)rows * Kp;
+    if (need <= b->ws_bytes && (size_t)rows <= b->ws_rows) return QLINEAR_OK;
+    size_t bytes = std::max(need, b->ws_bytes);
+    size_t nrows = std::max((size_t)rows, b->ws_rows);
+    nrows = (nrows + 255) / 256 * 256;
+    bytes = std::max(bytes, nrows * (size_t)std::max(Kp, b->max_kp));
+    bytes = (bytes + 4095) / 4096 * 4096;
+    cudaFree(b->d_ws);
+    cudaFree(b->d_ascale);
+    cudaFree(b->d_rowsum);
+    b->d_ws = nullptr;
+    b->d_ascale = nullptr;
+    b->d_rowsum = nullptr;
+    b->ws_bytes = 0;
+    b->ws_rows = 0;
+    b->amaps.clear();
+    QL_TRY(cudaMalloc(&b->d_ws, bytes));
+    QL_TRY(cudaMalloc(&b->d_ascale, nrows * sizeof(float)));
+    QL_TRY(cudaMalloc(&b->d_rowsum, nrows * sizeof(int32_t)));
+    b->ws_bytes = bytes;
+    b->ws_rows = nrows;
+    return QLINEAR_OK;
+}
+
+int ensure_dev(void **p, size_t *cap, size_t need) {
+    if (need <= *cap) return QLINEAR_OK;
+    cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    need = (need + 4095) / 4096 * 4096;
+    QL_TRY(cudaMalloc(p, need));
+    *cap = need;
+    return QLINEAR_OK;
+}
+
+int ensure_host(void **p, size_t *cap, size_t need) {
+    if (need <= *cap) return QLINEAR_OK;
+    cudaFreeHost(*p);
+    *p = nullptr;
+    *cap = 0;
+    need = (need + 4095) / 4096 * 4096;
+    QL_TRY(cudaMallocHost(p, need));
+    *cap = need;
+    return QLINEAR_OK;
+}
+
+int get_amap(qlinear_backend *b, int Kp, int tok, const CUtensorMap **out) {
+    const int rows_cap = (int)std::min<size_t>(b->ws_bytes / Kp, 1u << 30);
+    auto key = std::make_tuple((const void *)b->d_ws, Kp, tok, (size_t)rows_cap);
+    auto it = b->amaps.find(key);
+    if (it == b->amaps.end()) {
+        CUtensorMap m;
+        if (!encode_act_map(reinterpret_cast<const int8_t *>(b->d_ws), rows_cap, Kp, tok, &m))
+            return QLINEAR_ERR_CUDA;
+        it = b->amaps.emplace(key, m).first;
+    }
+    *out = &it->second;
+    return QLINEAR_OK;
+}
+
+bool valid_io_type(int t) { return t == QLINEAR_F32 || t == QLINEAR_F16; }
+
+int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_dev, int a_type,
+                    void *c_dev, int c_type, long long ldc, int rows, unsigned flags,
+                    cudaStream_t stream) {
+    const WeightView &v = w->view;
+    const bool swiglu = (flags & QLINEAR_RUN_SWIGLU) != 0;
+    const int width = swiglu ? v.N / 2 : v.N;
+    if (rows < 1 || !a_dev || !c_dev || !valid_io_type(a_type)) return QLINEAR_ERR_PARAM;
+    if (c_type != QLINEAR_F32 && c_type != QLINEAR_F16 && c_type != QLINEAR_I32)
+        return QLINEAR_ERR_PARAM;
+    if (swiglu && (v.N % 2 != 0 || c_type == QLINEAR_I32)) return QLINEAR_ERR_PARAM;
+    if (ldc < width) return QLINEAR_ERR_PARAM;
+    if ((flags & ~QLINEAR_RUN_SWIGLU) != 0) return QLINEAR_ERR_PARAM;
+
+    int st = ensure_act_ws(b, rows, v.Kp);
+    if (st) return st;
+    int8_t *codes = reinterpret_cast<int8_t *>(b->d_ws);
+    QL_TRY(launch_act_quant(a_dev, a_type, v.K, rows, v.K, v.Kp, b->round_mode, codes, b->d_ascale,
+                            b->d_rowsum, stream));
+    b->launches++;
+    ActView av{codes, b->d_ascale, b->d_rowsum, (int)(b->ws_bytes / v.Kp)};
+
+    if (rows <= 8) {
+        QL_TRY(launch_gemv(v, av, rows, c_dev, c_type, ldc, swiglu, b->num_sms, stream));
+        b->launches++;
+        b->gemv_calls++;
+        return QLINEAR_OK;
+    }
+    const GemmPlan plan = plan_gemm(v, rows, b->num_sms);
+    const CUtensorMap *amap = nullptr;
+    st = get_amap(b, v.Kp, plan.tok, &amap);
+    if (st) return st;
+    if (!swiglu) {
+        QL_TRY(launch_gemm(v, w->wmap, av, *amap, plan, rows, c_dev, c_type, ldc, b->d_err, stream));
+        b->launches++;
+    } else {
+        st = ensure_dev(reinterpret_cast<void **>(&b->d_y), &b->y_elems,
+                        (size_t)rows * v.N * sizeof(float));
+        if (st) return st;
+        QL_TRY(launch_gemm(v, w->wmap, av, *amap, plan, rows, b->d_y, kF32, v.N, b->d_err, stream));
+        QL_TRY(launch_swiglu(b->d_y, rows, v.N, c_dev, c_type, ldc, stream));
+        b->launches += 2;
+    }
+    b->gemm_calls++;
+    return QLINEAR_OK;
+}
+
+qlinear_weights *weights_create_common(qlinear_backend *b, const qlinear_weight_config *cfg,
+                                       const void *src, size_t src_bytes, const float *scales,
+                                       int n_total, int n_begin, int n_end, bool checkpoint) {
+    if (!b || !cfg || !src || !scales) return fail(QLINEAR_ERR_PARAM), nullptr;
+    if ((cfg->bits != 4 && cfg->bits != 8) || cfg->K <= 0 || cfg->N <= 0 || cfg->K > kMaxK)
+        return fail(QLINEAR_ERR_PARAM), nullptr;
+    if (n_begin < 0 || n_end > n_total || n_begin >= n_end) return fail(QLINEAR_ERR_PARAM), nullptr;
+    const int N = n_end - n_begin;
+    for (int n = n_begin; n < n_end; n++)
+        if (!(scales[n] > 0.0f) || !(scales[n] < INFINITY))  // src/model/checkpoint.rs:334-337
+            return fail(QLINEAR_ERR_PARAM), nullptr;
+    DeviceGuard guard(b->device);
+    auto *w = new (std::nothrow) qlinear_weights();
+    if (!w) return fail(QLINEAR_ERR_ALLOC), nullptr;
+    w->backend = b;
+    WeightView &v = w->view;
+    v.bits = cfg->bits;
+    v.K = cfg->K;
+    v.N = N;
+    v.Kp = (int)round_up(cfg->K, KBLK);
+    v.Np = (int)round_up(N, CH_TILE);
+    const size_t wbytes = (size_t)v.Np * (v.bits == 8 ? v.Kp : v.Kp / 2);
+    void *tmp = nullptr;
+    auto cleanup = [&](int status) -> qlinear_weights * {
+        cudaFree(tmp);
+        cudaFree(w->d_w);
+        cudaFree(w->d_s);
+        delete w;
+        fail(status);
+        return nullptr;
+    };
+    cudaError_t e;
+    if ((e = cudaMalloc(&w->d_w, wbytes)) != cudaSuccess) return cleanup(cuda_status(e));
+    if ((e = cudaMalloc(&w->d_s, (size_t)v.Np * sizeof(float))) != cudaSuccess)
+        return cleanup(cuda_status(e));
+    if ((e = cudaMemsetAsync(w->d_s, 0, (size_t)v.Np * sizeof(float), b->stream)) != cudaSuccess)
+        return cleanup(cuda_status(e));
+    if ((e = cudaMemcpyAsync(w->d_s, scales + n_begin, (size_t)N * sizeof(float),
+                             cudaMemcpyHostToDevice, b->stream)) != cudaSuccess)
+        return cleanup(cuda_status(e));
+    if ((e = cudaMalloc(&tmp, src_bytes)) != cudaSuccess) return cleanup(cuda_status(e));
+    if ((e = cudaMemcpyAsync(tmp, src, src_bytes, cudaMemcpyHostToDevice, b->stream)) != cudaSuccess)
+        return cleanup(cuda_status(e));
+    v.w = w->d_w;
+    v.scales = w->d_s;
+    if (checkpoint)
+        e = launch_pack_from_checkpoint(tmp, v, w->d_w, b->stream);
+    else
+        e = launch_pack_from_kn(static_cast<const int8_t *>(tmp), cfg->K, n_total, n_begin, v,
+                                w->d_w, b->stream);
+    if (e != cudaSuccess) return cleanup(cuda_status(e));
+    b->launches++;
+    if ((e = cudaStreamSynchronize(b->stream)) != cudaSuccess) return cleanup(cuda_status(e));
+    cudaFree(tmp);
+    tmp = nullptr;
+    if (!encode_weight_map(v, &w->wmap)) return cleanup(QLINEAR_ERR_CUDA);
+    w->bytes = wbytes + (uint64_t)v.Np * sizeof(float);
+    b->weight_bytes += w->bytes;
+    (v.bits == 4 ? b->loaded_w4 : b->loaded_w8)++;
+    b->max_kp = std::max(b->max_kp, v.Kp);
+    b->max_n = std::max(b->max_n, v.N);
+    return w;
+}
+
+}  // namespace
+
+// ====================================================================== C ABI
+extern "C" {
+
+void qlinear_backend_config_init(qlinear_backend_config *cfg) {
+    if (!cfg) return;
+    std::memset(cfg, 0, sizeof(*cfg));
+    cfg->device = 0;
+    cfg->round_mode = QLINEAR_ROUND_AWAY;
+    cfg->max_rows = 256;
+}
+
+qlinear_backend *qlinear_backend_create(const qlinear_backend_config *cfg) {
+    qlinear_backend_config def;
+    qlinear_backend_config_init(&def);
+    if (!cfg) cfg = &def;
+    if (cfg->round_mode != QLINEAR_ROUND_AWAY && cfg->round_mode != QLINEAR_ROUND_EVEN)
+        return fail(QLINEAR_ERR_PARAM), nullptr;
+    if (cfg->max_rows < 0) return fail(QLINEAR_ERR_PARAM), nullptr;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || cfg->device < 0 || cfg->device >= ndev)
+        return fail(ndev == 0 ? QLINEAR_ERR_CUDA : QLINEAR_ERR_PARAM), nullptr;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, cfg->device) != cudaSuccess)
+        return fail(QLINEAR_ERR_CUDA), nullptr;
+    if (prop.major != 10 || prop.minor != 0) return fail(QLINEAR_ERR_UNSUPPORTED), nullptr;
+    if (!tma_available()) return fail(QLINEAR_ERR_UNSUPPORTED), nullptr;
+    DeviceGuard guard(cfg->device);
+    auto *b = new (std::nothrow) qlinear_backend();
+    if (!b) return fail(QLINEAR_ERR_ALLOC), nullptr;
+    b->device = cfg->device;
+    b->round_mode = cfg->round_mode;
+    b->num_sms = prop.multiProcessorCount;
+    b->prepared_rows = cfg->max_rows ? cfg->max_rows : 256;
+    if (cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&b->d_err, sizeof(unsigned)) != cudaSuccess ||
+        cudaMallocHost(&b->h_err, sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(b->d_err, 0, sizeof(unsigned)) != cudaSuccess) {
+        qlinear_backend_free(b);
+        return fail(QLINEAR_ERR_CUDA), nullptr;
+    }
+    return b;
+}
+
+void qlinear_backend_free(qlinear_backend *b) {
+    if (!b) return;
+    DeviceGuard guard(b->device);
+    if (b->stream) cudaStreamSynchronize(b->stream);
+    cudaFree(b->d_ws);
+    cudaFree(b->d_ascale);
+    cudaFree(b->d_rowsum);
+    cudaFree(b->d_y);
+    cudaFree(b->d_in);
+    cudaFree(b->d_out);
+    cudaFree(b->d_err);
+    cudaFreeHost(b->h_in);
+    cudaFreeHost(b->h_out);
+    cudaFreeHost(b->h_err);
+    if (b->stream) cudaStreamDestroy(b->stream);
+    delete b;
+}
+
+qlinear_weights *qlinear_weights_create(qlinear_backend *b, const qlinear_weight_config *cfg,
+                                        const int8_t *codes_kn, const float *scales) {
+    if (!cfg) return fail(QLINEAR_ERR_PARAM), nullptr;
+    return weights_create_common(b, cfg, codes_kn, (size_t)cfg->K * cfg->N, scales, cfg->N, 0,
+                                 cfg->N, false);
+}
+
+qlinear_weights *qlinear_weights_create_shard(qlinear_backend *b, const qlinear_weight_config *cfg,
+                                              const int8_t *codes_kn, const float *scales,
+                                              int n_begin, int n_end) {
+    if (!cfg) return fail(QLINEAR_ERR_PARAM), nullptr;
+    return weights_create_common(b, cfg, codes_kn, (size_t)cfg->K * cfg->N, scales, cfg->N, n_begin,
+                                 n_end, false);
+}
+
+qlinear_weights *qlinear_weights_create_checkpoint(qlinear_backend *b,
+                                                   const qlinear_weight_config *cfg,
+                                                   const void *storage, const float *scales) {
+    if (!cfg || cfg->K <= 0 || cfg->N <= 0) return fail(QLINEAR_ERR_PARAM), nullptr;
+    const size_t bytes = cfg->bits == 4 ? (size_t)cfg->N * ((cfg->K + 7) / 8) * 4
+                                        : (size_t)cfg->N * cfg->K;
+    return weights_create_common(b, cfg, storage, bytes, scales, cfg->N, 0, cfg->N, true);
+}
+
+int qlinear_weights_query(const qlinear_weights *w, qlinear_weight_info *info) {
+    if (!w || !info) return QLINEAR_ERR_PARAM;
+    info->bits = w->view.bits;
+    info->K = w->view.K;
+    info->N = w->view.N;
+    info->K_padded = w->view.Kp;
+    info->N_padded = w->view.Np;
+    info->device_bytes = w->bytes;
+    return QLINEAR_OK;
+}
+
+void qlinear_weights_free(qlinear_weights *w) {
+    if (!w) return;
+    qlinear_backend *b = w->backend;
+    DeviceGuard guard(b->device);
+    cudaStreamSynchronize(b->stream);
+    cudaFree(w->d_w);
+    cudaFree(w->d_s);
+    b->weight_bytes -= w->bytes;
+    (w->view.bits == 4 ? b->loaded_w4 : b->loaded_w8)--;
+    delete w;
+}
+
+int qlinear_backend_prepare(qlinear_backend *b, int rows) {
+    if (!b || rows < 1) return QLINEAR_ERR_PARAM;
+    DeviceGuard guard(b->device);
+    b->prepared_rows = std::max(b->prepared_rows, rows);
+    if (b->max_kp == 0) return QLINEAR_OK;
+    int st = ensure_act_ws(b, rows, b->max_kp);
+    if (st) return st;
+    if (rows > 8)
+        st = ensure_dev(reinterpret_cast<void **>(&b->d_y), &b->y_elems,
+                        (size_t)rows * b->max_n * sizeof(float));
+    return st;
+}
+
+int qlinear_run_device(qlinear_backend *b, const qlinear_weights *w, const void *a_dev, int a_type,
+                       void *c_dev, int c_type, long long ldc, int rows, unsigned flags,
+                       void *stream) {
+    if (!b || !w || w->backend != b) return QLINEAR_ERR_PARAM;
+    DeviceGuard guard(b->device);
+    return run_device_impl(b, w, a_dev, a_type, c_dev, c_type, ldc, rows, flags,
+                           static_cast<cudaStream_t>(stream));
+}
+
+static int run_host(qlinear_backend *b, const qlinear_weights *w, const float *a_host,
+                    float *c_host, int rows, unsigned flags) {
+    if (!b || !w || w->backend != b || !a_host || !c_host || rows < 1) return QLINEAR_ERR_PARAM;
+    DeviceGuard guard(b->device);
+    const WeightView &v = w->view;
+    const bool swiglu = (flags & QLINEAR_RUN_SWIGLU) != 0;
+    if (swiglu && v.N % 2) return QLINEAR_ERR_PARAM;
+    const int width = swiglu ? v.N / 2 : v.N;
+    const size_t in_bytes = (size_t)rows * v.K * sizeof(float);
+    const size_t out_bytes = (size_t)rows * width * sizeof(float);
+    int st;
+    if ((st = ensure_host(&b->h_in, &b->h_in_bytes, in_bytes)) ||
+        (st = ensure_host(&b->h_out, &b->h_out_bytes, out_bytes)) ||
+        (st = ensure_dev(&b->d_in, &b->d_in_bytes, in_bytes)) ||
+        (st = ensure_dev(&b->d_out, &b->d_out_bytes, out_bytes)))
+        return st;
+    std::memcpy(b->h_in, a_host, in_bytes);
+    QL_TRY(cudaMemcpyAsync(b->d_in, b->h_in, in_bytes, cudaMemcpyHostToDevice, b->stream));
+    st = run_device_impl(b, w, b->d_in, QLINEAR_F32, b->d_out, QLINEAR_F32, width, rows, flags,
+                         b->stream);
+    if (st) return st;
+    QL_TRY(cudaMemcpyAsync(b->h_out, b->d_out, out_bytes, cudaMemcpyDeviceToHost, b->stream));
+    QL_TRY(cudaMemcpyAsync(b->h_err, b->d_err, sizeof(unsigned), cudaMemcpyDeviceToHost, b->stream));
+    QL_TRY(cudaStreamSynchronize(b->stream));
+    if (*b->h_err) {
+        cudaMemsetAsync(b->d_err, 0, sizeof(unsigned), b->stream);
+        cudaStreamSynchronize(b->stream);
+        return QLINEAR_ERR_TIMEOUT;
+    }
+    std::memcpy(c_host, b->h_out, out_bytes);
+    return QLINEAR_OK;
+}
+
+int qlinear_run_f32(qlinear_backend *b, const qlinear_weights *w, const float *a_host,
+                    float *c_host, int rows) {
+    return run_host(b, w, a_host, c_host, rows, 0);
+}
+
+int qlinear_run_swiglu_f32(qlinear_backend *b, const qlinear_weights *w, const float *a_host,
+                           float *c_host, int rows) {
+    return run_host(b, w, a_host, c_host, rows, QLINEAR_RUN_SWIGLU);
+}
+
+int qlinear_act_quant_device(qlinear_backend *b, const void *a_dev, int a_type, int rows, int K,
+                             int8_t *codes_dev, float *scales_dev, int32_t *rowsums_dev,
+                             void *stream) {
+    if (!b || !a_dev || !codes_dev || !scales_dev || rows < 1 || K < 1 || !valid_io_type(a_type))
+        return QLINEAR_ERR_PARAM;
+    DeviceGuard guard(b->device);
+    QL_TRY(launch_act_quant(a_dev, a_type, K, rows, K, K, b->round_mode, codes_dev, scales_dev,
+                            rowsums_dev, static_cast<cudaStream_t>(stream)));
+    b->launches++;
+    return QLINEAR_OK;
+}
+
+int qlinear_backend_check(qlinear_backend *b, void *stream) {
+    if (!b) return QLINEAR_ERR_PARAM;
+    DeviceGuard guard(b->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    QL_TRY(cudaStreamSynchronize(s));
+    QL_TRY(cudaMemcpy(b->h_err, b->d_err, sizeof(unsigned), cudaMemcpyDeviceToHost));
+    if (*b->h_err) {
+        QL_TRY(cudaMemset(b->d_err, 0, sizeof(unsigned)));
+        return QLINEAR_ERR_TIMEOUT;
+    }
+    return QLINEAR_OK;
+}
+
+int qlinear_backend_stats(const qlinear_backend *b, char *buf, size_t len) {
+    if (!b) return QLINEAR_ERR_PARAM;
+    const size_t ws = b->ws_bytes + b->ws_rows * 8 + b->y_elems + b->d_in_bytes + b->d_out_bytes;
+    char tmp[1024];
+    const int n = std::snprintf(
+        tmp, sizeof(tmp),
+        "{\"backend\": \"cuda-sm100a\", \"device\": %d, \"sm_count\": %d, \"loaded_w4\": %d, "
+        "\"loaded_w8\": %d, \"weight_payload_bytes\": %llu, \"workspace_payload_bytes\": %llu, "
+        "\"workspace_count\": %d, \"host_staging_bytes\": %llu, \"tune_cache_hits\": 0, "
+        "\"tune_cache_misses\": 0, \"tune_calls\": 0, \"strategy_fallbacks\": 0, "
+        "\"strategy_fallback_calls\": 0, \"weight_reload_calls\": 0, \"round_mode\": \"%s\", "
+        "\"prepared_rows\": %d, \"kernel_launches\": %llu, \"gemv_calls\": %llu, "
+        "\"gemm_calls\": %llu}",
+        b->device, b->num_sms, b->loaded_w4, b->loaded_w8, (unsigned long long)b->weight_bytes,
+        (unsigned long long)ws, b->ws_bytes ? 1 : 0,
+        (unsigned long long)(b->h_in_bytes + b->h_out_bytes),
+        b->round_mode == QLINEAR_ROUND_AWAY ? "away" : "even", b->prepared_rows, b->launches,
+        b->gemv_calls, b->gemm_calls);
+    if (n < 0) return QLINEAR_ERR_PARAM;
+    if (buf && len) {
+        std::strncpy(buf, tmp, len - 1);
+        buf[len - 1] = 0;
+    }
+    return n;
+}
+
+unsigned long long qlinear_backend_launches(const qlinear_backend *b) { return b ? b->launches : 0; }
+
+const char *qlinear_strerror(int status) {
+    switch (status) {
+    case QLINEAR_OK: return "ok";
+    case QLINEAR_ERR_PARAM: return "invalid argument";
+    case QLINEAR_ERR_ALLOC: return "allocation failed";
+    case QLINEAR_ERR_CUDA: return "CUDA error";
+    case QLINEAR_ERR_UNSUPPORTED: return "unsupported";
+    case QLINEAR_ERR_TIMEOUT: return "device wait timed out";
+    case QLINEAR_ERR_NCCL: return "NCCL error";
+    case QLINEAR_ERR_STATE: return "invalid state";
+    default: return "unknown status";
+    }
+}
+
+int qlinear_last_status(void) { return g_last_status; }
+
+const char *qlinear_version(void) { return "qlinear-b200 0.1.0 (sm_100a)"; }
+
+}  // extern "C"
