@@ -1,0 +1,485 @@
+#!/usr/bin/env python3
+"""Benchmark of the quantized-linear hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload cfg4|cfg0|cfg1|cfg2|...]
+
+Headline workload (default ``cfg4``): the W4A8 linear K=8192, N=28672 at M=512 tokens,
+split column-parallel over N GPUs (each rank owns N/g output channels), followed by an
+NCCL all-gather of the fp16 outputs and the [g][M][N/g] -> [M][N] assembly.  A step is
+one pass of the path over one batch: act-quant -> tcgen05 GEMM -> (all-gather ->
+assembly).  ``value`` is whole-job TOPS (2*M*K*N / step time, device-timed with CUDA
+events, max over ranks), inputs resident in HBM, L2 flushed between timed steps by a
+256 MiB write outside the timed region.  Scaling is strong (the layer is fixed).
+
+The line also carries: the decode half of the metric (W8A8 K=2560 N=9728 at M=1, GB/s,
+weights rotated through 8 copies so they come from HBM); the roofline of the dominant
+kernel; the CPU baseline (the C oracle, a bounded row sample, all host threads; rank 0,
+N=1); ``e2e`` through the reference-facing C-ABI call with host f32 buffers
+(qlinear_run_f32 at N=1; H2D -> run -> all-gather -> D2H at N>1); SM clocks sampled
+during the timed region.
+
+``--impl reference`` times the reference's CPU implementation of the path (the oracle
+restatement of src/npu.rs:1097-1121 -- the reference's Rust crate cannot be built here)
+on the same workload, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+# DRAM traffic of the dominant kernel per launch (dram__bytes_read.sum +
+# dram__bytes_write.sum) from the ncu capture summarised in
+# profiles/gemm_w4a8_cfg4_m512.md; None until a capture exists for this build.
+GEMM_TRAFFIC_BYTES = None
+
+WORKLOADS = {
+    # name: (bits, K, N, M, description)
+    "cfg4": (4, 8192, 28672, 512, "cfg4 W4A8 K8192 N28672 M512 split-N + all-gather"),
+    "cfg4_m8192": (4, 8192, 28672, 8192, "cfg4 W4A8 K8192 N28672 M8192 split-N + all-gather"),
+    "cfg0": (4, 2560, 9728, 512, "cfg0 W4A8 gate_proj K2560 N9728 M512"),
+    "cfg1": (8, 2560, 9728, 1, "cfg1 W8A8 decode K2560 N9728 M1"),
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg4")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+                    help="target CPU time of the oracle baseline sample")
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- helpers
+class ClockSampler:
+    """nvidia-smi samples (200 ms) of SM clock and throttle reasons while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except OSError:
+        return {}
+
+
+def int8_peak_tops(torch, dev) -> float:
+    """Dense int8 tensor-core throughput of cuBLASLt on this GPU (torch._int_mm, 8192^3,
+    best of 10 back-to-back launches): the int8 denominator MEASURED_PEAKS.json lacks."""
+    a = torch.randint(-127, 127, (8192, 8192), dtype=torch.int8, device=dev)
+    b = torch.randint(-127, 127, (8192, 8192), dtype=torch.int8, device=dev).t()
+    for _ in range(3):
+        torch._int_mm(a, b)
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(10):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._int_mm(a, b)
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1) * 1e-3)
+    del a, b
+    return 2 * 8192 ** 3 / best / 1e12
+
+
+def cpu_info():
+    model = ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    model = ln.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return os.cpu_count(), model
+
+
+def oracle_sample(bits, k, n, m_total, cpu_seconds, seed_stream=0, max_rows=None):
+    """Time the C oracle (all host threads) on a row sample sized to ~cpu_seconds.
+    Returns (ops_per_s, rows, seconds, threads)."""
+    from oracle import oracle as O
+    from open_rknpu2_lm_infer_b200 import workloads as W
+    O.build()
+    co = O.COracle()
+    threads = co.max_threads()
+    w = W.weight_codes(bits, k, n)
+    sw = W.weight_scales(n)
+    x = W.activations(m_total if max_rows is None else min(m_total, max_rows), k)
+    # probe with one row (warm), then size the sample
+    co.linear(w, sw, x[:1])
+    t0 = time.perf_counter()
+    co.linear(w, sw, x[:1])
+    t1 = time.perf_counter() - t0
+    rows = int(max(1, min(x.shape[0], cpu_seconds / max(t1, 1e-6))))
+    t0 = time.perf_counter()
+    co.linear(w, sw, x[:rows])
+    dt = time.perf_counter() - t0
+    return 2.0 * rows * k * n / dt, rows, dt, threads
+
+
+# ----------------------------------------------------------------------------- arms
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU implementation of the path (oracle port)."""
+    if rank != 0:
+        return
+    bits, k, n, m, desc = WORKLOADS[args.workload]
+    from oracle import oracle as O
+    from open_rknpu2_lm_infer_b200 import workloads as W
+    O.build()
+    co = O.COracle()
+    threads = co.max_threads()
+    w = W.weight_codes(bits, k, n)
+    sw = W.weight_scales(n)
+    x = W.activations(m, k)
+    co.linear(w, sw, x[:1])
+    t0 = time.perf_counter()
+    co.linear(w, sw, x[:1])
+    t1 = time.perf_counter() - t0
+    # each step: a bounded row sample so that warmup + steps stay within ~2 minutes
+    budget = 100.0 / max(1, args.steps + args.warmup)
+    rows = int(max(1, min(m, budget / max(t1, 1e-6))))
+    for _ in range(args.warmup):
+        co.linear(w, sw, x[:rows])
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        co.linear(w, sw, x[:rows])
+        times.append(time.perf_counter() - t0)
+    dt = sum(times) / len(times)
+    tops = 2.0 * rows * k * n / dt / 1e12
+    cores, model = cpu_info()
+    sample = f"{rows} of {m} rows per step ({desc}), C oracle, {threads} OpenMP threads, {model}"
+    line = {
+        "impl": "reference", "metric": "W4A8 linear TOPS (M=512) & decode GB/s (M=1), % of roofline, at 1/2/4/8 B200",
+        "value": tops, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt * 1e3 * m / rows,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic",
+        "config": {"workload": desc, "M": m, "K": k, "N": n, "bits": bits},
+        "cpu_baseline": {"value": tops, "unit": "TOPS", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": tops, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from open_rknpu2_lm_infer_b200 import Backend, QuantMatrix
+    from open_rknpu2_lm_infer_b200 import workloads as W
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    bits, k, n, m, desc = WORKLOADS[args.workload]
+    assert n % world == 0 and (n // world) % 8 == 0
+    ns = n // world
+    n0 = rank * ns
+
+    backend = Backend(device=local_rank)
+    codes = W.weight_codes(bits, k, n)
+    scales = W.weight_scales(n)
+    lin = backend.load_shard(QuantMatrix(bits, k, n, codes, scales), n0, n0 + ns)
+    del codes
+    backend.prepare(m)
+    x_host = W.activations(m, k)
+    x = torch.from_numpy(x_host).to(dev)
+    y_local = torch.empty((m, ns), dtype=torch.float16, device=dev)
+    y_gather = torch.empty((world, m, ns), dtype=torch.float16, device=dev) if world > 1 else None
+    y_full = torch.empty((m, n), dtype=torch.float16, device=dev) if world > 1 else y_local
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+
+    def step():
+        lin.run_device(x, y_local, m, stream=stream)
+        if world > 1:
+            dist.all_gather_into_tensor(y_gather, y_local)
+            backend.interleave_columns(y_gather, y_full, world, m, ns, 2, stream=stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    launches0 = backend.launches()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    backend.check(stream)
+
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    backend.profile(True)
+    barrier()
+    torch.cuda.synchronize(dev)
+    launches_before = backend.launches()
+    times = []
+    # Hold the GPU while the host enqueues every timed step, so the events measure device
+    # time only (no host launch gaps inside a step).
+    torch.cuda._sleep(int(2e8))
+    for _ in range(args.steps):
+        flush.zero_()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step()
+        e1.record()
+        times.append((e0, e1))
+    torch.cuda.synchronize(dev)
+    barrier()
+    launches_timed = backend.launches() - launches_before
+    clocks = sampler.stop()
+    backend.profile(False)
+    quant_ms, main_ms, calls = backend.profile_collect()
+    backend.check(stream)
+    step_s = sum(a.elapsed_time(b) for a, b in times) * 1e-3
+    t = torch.tensor([step_s, main_ms * 1e-3, quant_ms * 1e-3], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_s, main_s, quant_s = t.tolist()
+    mean_step = step_s / args.steps
+    ops = 2.0 * m * k * n
+    value = ops / mean_step / 1e12
+
+    # roofline of the dominant kernel (the GEMM on this rank's shard)
+    per_launch = main_s / max(calls, 1)
+    shard_ops = 2.0 * m * k * ns
+    int8_peak = int8_peak_tops(torch, dev)
+    achieved = shard_ops / per_launch / 1e12
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TFLOP/s",
+                "frac": achieved / int8_peak,
+                "peak_source": "int8 dense, measured by bench.py: cuBLASLt (torch._int_mm) "
+                               "8192^3 burst; MEASURED_PEAKS.json has no int8 figure",
+                "frac_of_nominal_4500": achieved / 4500.0,
+                "traffic": GEMM_TRAFFIC_BYTES,
+                "kernel": "gemm_kernel<4> (tcgen05 kind::i8)",
+                "kernel_ms": per_launch * 1e3, "act_quant_ms": quant_s / max(calls, 1) * 1e3}
+
+    line = {
+        "metric": "W4A8 linear TOPS (M=512) & decode GB/s (M=1), % of roofline, at 1/2/4/8 B200",
+        "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": mean_step * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": desc, "M": m, "K": k, "N": n, "bits": bits,
+                   "parallelism": f"split-N x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+                   "l2": "flushed (256 MiB write) between timed steps, outside the timed region",
+                   "inputs": "fp16 N(0,1) with 1% x20 outlier channels, seed 42"},
+        "roofline": roofline,
+        "gpu_launches": int(launches_timed),
+        "clocks": clocks,
+    }
+
+    # decode half of the metric: W8A8 K2560 N9728 M=1 (HBM-bound GEMV)
+    if not args.no_decode:
+        line["decode"] = decode_measure(backend, torch, dev, args, world)
+
+    # end to end through the public C ABI with host buffers
+    if not args.no_e2e:
+        line["e2e"] = e2e_measure(backend, lin, torch, dist, dev, args, world, m, k, n, ns,
+                                  x_host, y_gather)
+
+    if rank == 0 and world == 1:
+        ops_s, rows, dt, threads = oracle_sample(bits, k, n, m, args.cpu_seconds)
+        cores, model = cpu_info()
+        line["cpu_baseline"] = {
+            "value": ops_s / 1e12, "unit": "TOPS", "cores": threads, "kind": "port",
+            "sample": f"{rows} of {m} rows of {desc}: C oracle (oracle/qlinear_ref.c, OpenMP "
+                      f"{threads} threads, {model}), {dt:.1f} s"}
+    line["gpu_launches"] = int(launches_timed)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    lin.close()
+    backend.close()
+
+
+def decode_measure(backend, torch, dev, args, world):
+    from open_rknpu2_lm_infer_b200 import QuantMatrix
+    from open_rknpu2_lm_infer_b200 import workloads as W
+    bits, k, n, m = 8, 2560, 9728, 1
+    copies = 8  # 8 x 24.9 MB rotated: each call reads weights that are not in L2
+    lins = []
+    for c in range(copies):
+        lins.append(backend.load(QuantMatrix(bits, k, n, W.weight_codes(bits, k, n, stream=c),
+                                             W.weight_scales(n, stream=c))))
+    x = torch.from_numpy(W.activations(m, k, stream=5)).to(dev)
+    y = torch.empty((m, n), dtype=torch.float16, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    for i in range(3 * copies):
+        lins[i % copies].run_device(x, y, m, stream=stream)
+    torch.cuda.synchronize(dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    backend.profile(True)
+    iters = max(args.steps, 8 * copies)
+    torch.cuda._sleep(int(2e8))
+    for i in range(iters):
+        if i % copies == 0:
+            flush.zero_()
+        lins[i % copies].run_device(x, y, m, stream=stream)
+    torch.cuda.synchronize(dev)
+    backend.profile(False)
+    quant_ms, main_ms, calls = backend.profile_collect()
+    backend.check(stream)
+    per_gemv = main_ms * 1e-3 / calls
+    per_call = (quant_ms + main_ms) * 1e-3 / calls
+    wbytes = k * n * bits // 8 + 4 * n
+    algo = wbytes + 2 * m * k + 2 * m * n
+    hbm = measured_peaks().get("hbm_gbs", 6650.0)
+    for l in lins:
+        l.close()
+    return {"config": "cfg1 W8A8 K2560 N9728 M1 (8 rotated weight copies)",
+            "gemv_us": per_gemv * 1e6, "call_us": per_call * 1e6,
+            "value": algo / per_gemv / 1e9, "unit": "GB/s",
+            "roofline": {"bound": "hbm", "achieved": algo / per_gemv / 1e9, "peak": hbm,
+                         "unit": "GB/s", "frac": algo / per_gemv / 1e9 / hbm,
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"},
+            "call_gbs_incl_act_quant": algo / per_call / 1e9}
+
+
+def e2e_measure(backend, lin, torch, dist, dev, args, world, m, k, n, ns, x_host, y_gather):
+    """Same metric through the public API with host buffers: H2D of the f32 input, the
+    path, (all-gather), D2H of the f32 output, every step; wall-clock between host
+    synchronisations, max over ranks."""
+    xin = np.ascontiguousarray(x_host.astype(np.float32))
+    steps = max(3, min(args.steps, 10))
+    if world == 1:
+        out = np.empty((m, n), np.float32)
+        for _ in range(2):
+            lin.run(xin, out, m)
+        ts = []
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            lin.run(xin, out, m)
+            ts.append(time.perf_counter() - t0)
+        dt = statistics.median(ts)
+        h2d, d2h = m * k * 4, m * n * 4
+    else:
+        pin_in = torch.from_numpy(xin).pin_memory()
+        pin_out = torch.empty((m, n), dtype=torch.float32).pin_memory()
+        xd = torch.empty((m, k), dtype=torch.float32, device=dev)
+        yl = torch.empty((m, ns), dtype=torch.float32, device=dev)
+        yg = torch.empty((world, m, ns), dtype=torch.float32, device=dev)
+        yf = torch.empty((m, n), dtype=torch.float32, device=dev)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+
+        def one():
+            xd.copy_(pin_in, non_blocking=True)
+            lin.run_device(xd, yl, m, stream=stream)
+            dist.all_gather_into_tensor(yg, yl)
+            backend.interleave_columns(yg, yf, world, m, ns, 4, stream=stream)
+            pin_out.copy_(yf, non_blocking=True)
+            torch.cuda.synchronize(dev)
+        for _ in range(2):
+            one()
+        ts = []
+        for _ in range(steps):
+            dist.barrier()
+            t0 = time.perf_counter()
+            one()
+            ts.append(time.perf_counter() - t0)
+        dt = statistics.median(ts)
+        t = torch.tensor([dt], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = t.item()
+        h2d, d2h = m * k * 4, m * n * 4
+    return {"value": 2.0 * m * k * n / dt / 1e12, "unit": "TOPS", "ms_per_step": dt * 1e3,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "api": "qlinear_run_f32 (host f32 in/out)" if world == 1 else
+                   "H2D f32 -> qlinear_run_device -> NCCL all-gather -> "
+                   "qlinear_interleave_columns -> D2H f32"}
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpus != world and world > 1:
+        print(f"--gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

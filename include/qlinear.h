@@ -153,6 +153,23 @@ QLINEAR_API int qlinear_act_quant_device(qlinear_backend *backend, const void *a
                              int K, int8_t *codes_dev, float *scales_dev, int32_t *rowsums_dev,
                              void *stream);
 
+/* Column-parallel (split-N) output assembly: src holds `shards` slabs [rows][shard_cols]
+ * back to back (the layout an all-gather of per-rank outputs produces), dst is
+ * [rows][shards * shard_cols] with dst[m][s * shard_cols + j] = src[s][m][j].  elem_bytes
+ * is 2 (fp16) or 4 (f32).  Asynchronous on `stream`.  No reference counterpart. */
+QLINEAR_API int qlinear_interleave_columns(qlinear_backend *backend, const void *src, void *dst,
+                                           int shards, int rows, int shard_cols, int elem_bytes,
+                                           void *stream);
+
+/* Per-kernel device timing (the role of the `timings` argument of rk_npu_w4a8_run_f32,
+ * src/npu.rs:1047): while enabled, every run records CUDA events around its activation
+ * quantisation and around its main kernel (GEMM or GEMV) on the call's stream.
+ * qlinear_backend_profile_collect synchronizes those events, returns the summed
+ * milliseconds and the number of calls, and clears the record. */
+QLINEAR_API int qlinear_backend_profile(qlinear_backend *backend, int enable);
+QLINEAR_API int qlinear_backend_profile_collect(qlinear_backend *backend, double *quant_ms,
+                                                double *main_ms, int *calls);
+
 /* Reads and clears the backend's device error word (bounded waits that gave up);
  * synchronizes `stream` first.  Returns QLINEAR_OK or QLINEAR_ERR_TIMEOUT. */
 QLINEAR_API int qlinear_backend_check(qlinear_backend *backend, void *stream);

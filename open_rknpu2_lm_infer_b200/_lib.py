@@ -65,6 +65,11 @@ SIGNATURES = {
     "qlinear_run_swiglu_f32": (_I, [_P, _P, _P, _P, _I]),
     "qlinear_run_device": (_I, [_P, _P, _P, _I, _P, _I, ctypes.c_longlong, _I, ctypes.c_uint, _P]),
     "qlinear_act_quant_device": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _P]),
+    "qlinear_interleave_columns": (_I, [_P, _P, _P, _I, _I, _I, _I, _P]),
+    "qlinear_backend_profile": (_I, [_P, _I]),
+    "qlinear_backend_profile_collect": (_I, [_P, ctypes.POINTER(ctypes.c_double),
+                                             ctypes.POINTER(ctypes.c_double),
+                                             ctypes.POINTER(ctypes.c_int)]),
     "qlinear_backend_check": (_I, [_P, _P]),
     "qlinear_backend_stats": (_I, [_P, ctypes.c_char_p, ctypes.c_size_t]),
     "qlinear_backend_launches": (ctypes.c_ulonglong, [_P]),

@@ -277,9 +277,18 @@ template <int BITS, typename OutT>
 cudaError_t launch_t(const CUtensorMap &wmap, const CUtensorMap &amap, const GemmArgs &args,
                      const GemmPlan &plan, cudaStream_t stream) {
     auto kern = gemm_kernel<BITS, OutT>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         plan.smem_bytes);
-    if (e != cudaSuccess) return e;
+    // The opt-in shared-memory limit is a per-device, per-kernel attribute: set it to the
+    // maximum once per device (an attribute call per launch costs host time).
+    static int configured[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             MAX_DYN_SMEM);
+        if (e != cudaSuccess) return e;
+        configured[dev] = 1;
+    }
     kern<<<plan.grid, gemm_threads<BITS>(), plan.smem_bytes, stream>>>(wmap, amap, args);
     return cudaGetLastError();
 }

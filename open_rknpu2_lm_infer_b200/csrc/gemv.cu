@@ -201,11 +201,17 @@ cudaError_t launch_t(const WeightView &w, const ActView &a, int rows, OutT *out,
     if (grid < 1) grid = 1;
     const size_t smem = (size_t)MT * w.Kp;
     auto kern = gemv_kernel<BITS, MT, ROWS, SWIGLU, OutT>;
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
+    static int configured[64] = {0};  // per device: raise the opt-in limit once
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!configured[dev]) {
+        cudaError_t e =
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         if (e != cudaSuccess) return e;
+        configured[dev] = 1;
     }
+    if (smem > 227 * 1024) return cudaErrorInvalidValue;
     kern<<<grid, kThreads, smem, stream>>>(w.w, w.scales, w.N, w.Np, w.Kp, a.codes, a.scales,
                                            a.rowsums, rows, out, ldc);
     return cudaGetLastError();

@@ -61,6 +61,10 @@ cudaError_t launch_gemm(const WeightView &w, const CUtensorMap &wmap, const ActV
 cudaError_t launch_swiglu(const float *y, int rows, int N, void *out, int out_type,
                           long long ldc, cudaStream_t stream);
 
+// dst[m][s*shard_cols + j] = src[s][m][j] (split-N output assembly).
+cudaError_t launch_interleave(const void *src, void *dst, int shards, int rows, int shard_cols,
+                              int elem_bytes, int num_sms, cudaStream_t stream);
+
 // TMA descriptor encoding through the driver entry point (no -lcuda link needed).
 bool tma_available();
 bool encode_weight_map(const WeightView &w, CUtensorMap *map);

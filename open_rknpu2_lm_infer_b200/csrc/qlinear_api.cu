@@ -23,6 +23,8 @@
 #include <new>
 #include <string>
 #include <tuple>
+#include <vector>
+#include <array>
 
 using namespace ql;
 
@@ -55,6 +57,10 @@ struct qlinear_backend {
     unsigned long long launches = 0;
     unsigned long long gemv_calls = 0, gemm_calls = 0;
     std::map<std::tuple<const void *, int, int, size_t>, CUtensorMap> amaps;
+    // per-kernel device timing (qlinear_backend_profile)
+    bool profiling = false;
+    std::vector<std::array<cudaEvent_t, 3>> prof_events;
+    size_t prof_used = 0;
 };
 
 struct qlinear_weights {
@@ -216,6 +222,17 @@ int get_amap(qlinear_backend *b, int Kp, int tok, const CUtensorMap **out) {
 
 bool valid_io_type(int t) { return t == QLINEAR_F32 || t == QLINEAR_F16; }
 
+int next_prof_events(qlinear_backend *b, const std::array<cudaEvent_t, 3> **out) {
+    if (b->prof_used == b->prof_events.size()) {
+        if (b->prof_events.size() >= 65536) return QLINEAR_ERR_STATE;  // collect first
+        std::array<cudaEvent_t, 3> e{};
+        for (auto &x : e) QL_TRY(cudaEventCreate(&x));
+        b->prof_events.push_back(e);
+    }
+    *out = &b->prof_events[b->prof_used++];
+    return QLINEAR_OK;
+}
+
 int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_dev, int a_type,
                     void *c_dev, int c_type, long long ldc, int rows, unsigned flags,
                     cudaStream_t stream) {
@@ -231,10 +248,23 @@ int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_
 
     int st = ensure_act_ws(b, rows, v.Kp);
     if (st) return st;
+    const std::array<cudaEvent_t, 3> *ev = nullptr;
+    if (b->profiling) {
+        if ((st = next_prof_events(b, &ev))) return st;
+        QL_TRY(cudaEventRecord((*ev)[0], stream));
+    }
     int8_t *codes = reinterpret_cast<int8_t *>(b->d_ws);
     QL_TRY(launch_act_quant(a_dev, a_type, v.K, rows, v.K, v.Kp, b->round_mode, codes, b->d_ascale,
                             b->d_rowsum, stream));
     b->launches++;
+    if (ev) QL_TRY(cudaEventRecord((*ev)[1], stream));
+    struct Stop {  // records the third event on every exit path below
+        const std::array<cudaEvent_t, 3> *ev;
+        cudaStream_t s;
+        ~Stop() {
+            if (ev) cudaEventRecord((*ev)[2], s);
+        }
+    } stop{ev, stream};
     ActView av{codes, b->d_ascale, b->d_rowsum, (int)(b->ws_bytes / v.Kp)};
 
     if (rows <= 8) {
@@ -385,6 +415,8 @@ void qlinear_backend_free(qlinear_backend *b) {
     cudaFreeHost(b->h_in);
     cudaFreeHost(b->h_out);
     cudaFreeHost(b->h_err);
+    for (auto &e : b->prof_events)
+        for (auto x : e) cudaEventDestroy(x);
     if (b->stream) cudaStreamDestroy(b->stream);
     delete b;
 }
@@ -510,6 +542,45 @@ int qlinear_act_quant_device(qlinear_backend *b, const void *a_dev, int a_type, 
     QL_TRY(launch_act_quant(a_dev, a_type, K, rows, K, K, b->round_mode, codes_dev, scales_dev,
                             rowsums_dev, static_cast<cudaStream_t>(stream)));
     b->launches++;
+    return QLINEAR_OK;
+}
+
+int qlinear_interleave_columns(qlinear_backend *b, const void *src, void *dst, int shards,
+                               int rows, int shard_cols, int elem_bytes, void *stream) {
+    if (!b || !src || !dst || shards < 1 || rows < 1 || shard_cols < 1 ||
+        (elem_bytes != 2 && elem_bytes != 4))
+        return QLINEAR_ERR_PARAM;
+    DeviceGuard guard(b->device);
+    QL_TRY(launch_interleave(src, dst, shards, rows, shard_cols, elem_bytes, b->num_sms,
+                             static_cast<cudaStream_t>(stream)));
+    b->launches++;
+    return QLINEAR_OK;
+}
+
+int qlinear_backend_profile(qlinear_backend *b, int enable) {
+    if (!b) return QLINEAR_ERR_PARAM;
+    b->profiling = enable != 0;
+    return QLINEAR_OK;
+}
+
+int qlinear_backend_profile_collect(qlinear_backend *b, double *quant_ms, double *main_ms,
+                                    int *calls) {
+    if (!b) return QLINEAR_ERR_PARAM;
+    DeviceGuard guard(b->device);
+    double q = 0, m = 0;
+    for (size_t i = 0; i < b->prof_used; i++) {
+        auto &e = b->prof_events[i];
+        QL_TRY(cudaEventSynchronize(e[2]));
+        float a = 0, c = 0;
+        QL_TRY(cudaEventElapsedTime(&a, e[0], e[1]));
+        QL_TRY(cudaEventElapsedTime(&c, e[1], e[2]));
+        q += a;
+        m += c;
+    }
+    if (quant_ms) *quant_ms = q;
+    if (main_ms) *main_ms = m;
+    if (calls) *calls = (int)b->prof_used;
+    b->prof_used = 0;
     return QLINEAR_OK;
 }
 

@@ -165,6 +165,25 @@ class Backend:
     def launches(self) -> int:
         return int(self._lib.qlinear_backend_launches(self.raw))
 
+    def profile(self, enable: bool) -> None:
+        """Per-kernel device timing (the reference's `timings` argument, src/npu.rs:1047)."""
+        _check(self._lib.qlinear_backend_profile(self.raw, 1 if enable else 0), "profile")
+
+    def profile_collect(self):
+        """(quant_ms_total, main_ms_total, calls) since the last collect."""
+        q, m, c = ctypes.c_double(), ctypes.c_double(), ctypes.c_int()
+        _check(self._lib.qlinear_backend_profile_collect(self.raw, ctypes.byref(q),
+                                                         ctypes.byref(m), ctypes.byref(c)),
+               "profile collect")
+        return q.value, m.value, c.value
+
+    def interleave_columns(self, src, dst, shards: int, rows: int, shard_cols: int,
+                           elem_bytes: int, stream=None) -> None:
+        """dst[m][s*shard_cols + j] = src[s][m][j] (split-N output assembly)."""
+        _check(self._lib.qlinear_interleave_columns(self.raw, _ptr(src), _ptr(dst), shards, rows,
+                                                    shard_cols, elem_bytes, stream),
+               "interleave columns")
+
     def check(self, stream=None) -> None:
         _check(self._lib.qlinear_backend_check(self.raw, stream), "device check")
 

@@ -138,26 +138,33 @@ int qref_act_quant_f16(const uint16_t *x, int64_t rows, int64_t k, int round_mod
     return 0;
 }
 
-/* Integer GEMM acc[m][n] = sum_k codes_a[m][k] * codes_w[k][n] (src/npu.rs:1111-1116). */
+/* Integer GEMM acc[m][n] = sum_k codes_a[m][k] * codes_w[k][n] (src/npu.rs:1111-1116).
+ * Blocked 16 rows x 256 columns so each 256-byte weight segment is reused from L1 by 16
+ * rows; integer sums are exact, so the blocking does not change any result. */
 int qref_int_gemm(const int8_t *qa, int64_t rows, int64_t k, const int8_t *w_kn, int64_t n,
                   int32_t *acc)
 {
     if (!qa || !w_kn || !acc || rows < 0 || k <= 0 || n <= 0) return -1;
-    const int64_t NB = 512; /* column block: keeps the i32 accumulators in L1 */
-    int64_t nblocks = (n + NB - 1) / NB;
+    enum { RB = 16, NB = 256 };
+    int64_t rblocks = (rows + RB - 1) / RB, nblocks = (n + NB - 1) / NB;
 #pragma omp parallel for collapse(2) schedule(static)
-    for (int64_t m = 0; m < rows; m++) {
+    for (int64_t rb = 0; rb < rblocks; rb++) {
         for (int64_t b = 0; b < nblocks; b++) {
-            int64_t n0 = b * NB, n1 = n0 + NB < n ? n0 + NB : n;
-            int32_t *out = acc + m * n;
-            for (int64_t j = n0; j < n1; j++) out[j] = 0;
-            const int8_t *a = qa + m * k;
+            int32_t tile[RB][NB];
+            int64_t r0 = rb * RB, r1 = r0 + RB < rows ? r0 + RB : rows;
+            int64_t n0 = b * NB, n1 = n0 + NB < n ? n0 + NB : n, w = n1 - n0;
+            memset(tile, 0, sizeof(tile));
             for (int64_t kk = 0; kk < k; kk++) {
-                int32_t q = a[kk];
-                if (q == 0) continue;
-                const int8_t *wr = w_kn + kk * n;
-                for (int64_t j = n0; j < n1; j++) out[j] += q * (int32_t)wr[j];
+                const int8_t *wr = w_kn + kk * n + n0;
+                for (int64_t r = r0; r < r1; r++) {
+                    int32_t q = qa[r * k + kk];
+                    if (q == 0) continue;
+                    int32_t *t = tile[r - r0];
+                    for (int64_t j = 0; j < w; j++) t[j] += q * (int32_t)wr[j];
+                }
             }
+            for (int64_t r = r0; r < r1; r++)
+                memcpy(acc + r * n + n0, tile[r - r0], sizeof(int32_t) * (size_t)w);
         }
     }
     return 0;
