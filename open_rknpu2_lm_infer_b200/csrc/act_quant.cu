@@ -30,13 +30,14 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kCache = 6;
 
+// 16-byte vector of the input type; kept raw (4 registers) in the row cache and widened
+// to f32 on use.
 template <typename T>
 struct Vec;
 template <>
 struct Vec<__half> {
     static constexpr int N = 8;
-    __device__ static __forceinline__ void load(const __half *p, float (&v)[8]) {
-        uint4 raw = *reinterpret_cast<const uint4 *>(p);
+    __device__ static __forceinline__ void widen(const uint4 &raw, float (&v)[8]) {
         const __half2 *h = reinterpret_cast<const __half2 *>(&raw);
 #pragma unroll
         for (int i = 0; i < 4; i++) {
@@ -49,9 +50,9 @@ struct Vec<__half> {
 template <>
 struct Vec<float> {
     static constexpr int N = 4;
-    __device__ static __forceinline__ void load(const float *p, float (&v)[4]) {
-        float4 raw = *reinterpret_cast<const float4 *>(p);
-        v[0] = raw.x; v[1] = raw.y; v[2] = raw.z; v[3] = raw.w;
+    __device__ static __forceinline__ void widen(const uint4 &raw, float (&v)[4]) {
+        v[0] = __uint_as_float(raw.x); v[1] = __uint_as_float(raw.y);
+        v[2] = __uint_as_float(raw.z); v[3] = __uint_as_float(raw.w);
     }
 };
 
@@ -115,20 +116,26 @@ __global__ void __launch_bounds__(kThreads) act_quant_vec_kernel(
     int8_t *cr = codes + m * (long long)Kp;
     const int nchunks = K / V;
 
-    float v[kCache][V];
+    // Let a dependent kernel launched with programmatic stream serialization start its
+    // prologue now; it waits (griddepcontrol.wait) before reading what this kernel writes.
+    asm volatile("griddepcontrol.launch_dependents;");
+    const uint4 *xv = reinterpret_cast<const uint4 *>(xr);
+    uint4 raw[kCache];
     float amax = 0.0f;
 #pragma unroll
     for (int i = 0; i < kCache; i++) {
         const int c = threadIdx.x + i * kThreads;
         if (c < nchunks) {
-            Vec<T>::load(xr + (long long)c * V, v[i]);
+            raw[i] = __ldg(xv + c);
+            float t[V];
+            Vec<T>::widen(raw[i], t);
 #pragma unroll
-            for (int e = 0; e < V; e++) amax = fmaxf(amax, fabsf(v[i][e]));
+            for (int e = 0; e < V; e++) amax = fmaxf(amax, fabsf(t[e]));
         }
     }
     for (int c = threadIdx.x + kCache * kThreads; c < nchunks; c += kThreads) {
         float t[V];
-        Vec<T>::load(xr + (long long)c * V, t);
+        Vec<T>::widen(__ldg(xv + c), t);
 #pragma unroll
         for (int e = 0; e < V; e++) amax = fmaxf(amax, fabsf(t[e]));
     }
@@ -137,7 +144,9 @@ __global__ void __launch_bounds__(kThreads) act_quant_vec_kernel(
     row_scale(amax, scale, inv);
 
     int sum = 0;
-    auto emit = [&](int c, const float(&t)[V]) {
+    auto emit = [&](int c, const uint4 &rv) {
+        float t[V];
+        Vec<T>::widen(rv, t);
         uint32_t w[V / 4];
 #pragma unroll
         for (int g = 0; g < V / 4; g++) {
@@ -158,13 +167,9 @@ __global__ void __launch_bounds__(kThreads) act_quant_vec_kernel(
 #pragma unroll
     for (int i = 0; i < kCache; i++) {
         const int c = threadIdx.x + i * kThreads;
-        if (c < nchunks) emit(c, v[i]);
+        if (c < nchunks) emit(c, raw[i]);
     }
-    for (int c = threadIdx.x + kCache * kThreads; c < nchunks; c += kThreads) {
-        float t[V];
-        Vec<T>::load(xr + (long long)c * V, t);
-        emit(c, t);
-    }
+    for (int c = threadIdx.x + kCache * kThreads; c < nchunks; c += kThreads) emit(c, __ldg(xv + c));
     for (int k = K + threadIdx.x; k < Kp; k += kThreads) cr[k] = 0;
     sum = block_sum(sum, redi);
     if (threadIdx.x == 0) {
@@ -180,6 +185,7 @@ __global__ void __launch_bounds__(kThreads) act_quant_scalar_kernel(
     int8_t *__restrict__ codes, float *__restrict__ scales, int32_t *__restrict__ rowsums) {
     __shared__ float redf[32];
     __shared__ int redi[32];
+    asm volatile("griddepcontrol.launch_dependents;");
     const long long m = blockIdx.x;
     const T *xr = x + m * ldx;
     int8_t *cr = codes + m * (long long)Kp;

@@ -53,9 +53,12 @@ struct GemmPlan {
     int tiles;
 };
 GemmPlan plan_gemm(const WeightView &w, int rows, int num_sms);
+// pdl: launch with programmatic stream serialization (the kernel waits with
+// griddepcontrol.wait before reading the activation codes / scales).
 cudaError_t launch_gemm(const WeightView &w, const CUtensorMap &wmap, const ActView &a,
                         const CUtensorMap &amap, const GemmPlan &plan, int rows, void *out,
-                        int out_type, long long ldc, unsigned *err, cudaStream_t stream);
+                        int out_type, long long ldc, unsigned *err, bool pdl,
+                        cudaStream_t stream);
 
 // SwiGLU over an f32 [rows][N] buffer: out[m][j] = silu(y[m][j]) * y[m][N/2 + j].
 cudaError_t launch_swiglu(const float *y, int rows, int N, void *out, int out_type,

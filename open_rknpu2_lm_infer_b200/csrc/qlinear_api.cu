@@ -145,14 +145,17 @@ bool tma_available() {
     load_encode();
     return g_encode != nullptr;
 }
+// The GEMM streams 64-deep k-blocks of 256-channel weight tiles (64-byte swizzle for the
+// 8-bit operands; packed W4 rows of 32 bytes are unpacked by the kernel itself).
 bool encode_weight_map(const WeightView &w, CUtensorMap *map) {
     if (w.bits == 8)
-        return encode_2d(map, w.w, w.Kp, w.Np, w.Kp, KBLK, CH_TILE, CU_TENSOR_MAP_SWIZZLE_128B);
-    return encode_2d(map, w.w, w.Kp / 2, w.Np, w.Kp / 2, KBLK / 2, CH_TILE,
+        return encode_2d(map, w.w, w.Kp, w.Np, w.Kp, GEMM_KB, 2 * CH_TILE,
+                         CU_TENSOR_MAP_SWIZZLE_64B);
+    return encode_2d(map, w.w, w.Kp / 2, w.Np, w.Kp / 2, GEMM_KB / 2, 2 * CH_TILE,
                      CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 bool encode_act_map(const int8_t *codes, int rows_cap, int Kp, int tok, CUtensorMap *map) {
-    return encode_2d(map, codes, Kp, rows_cap, Kp, KBLK, tok, CU_TENSOR_MAP_SWIZZLE_128B);
+    return encode_2d(map, codes, Kp, rows_cap, Kp, GEMM_KB, tok, CU_TENSOR_MAP_SWIZZLE_64B);
 }
 }  // namespace ql
 
@@ -278,13 +281,15 @@ int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_
     st = get_amap(b, v.Kp, plan.tok, &amap);
     if (st) return st;
     if (!swiglu) {
-        QL_TRY(launch_gemm(v, w->wmap, av, *amap, plan, rows, c_dev, c_type, ldc, b->d_err, stream));
+        QL_TRY(launch_gemm(v, w->wmap, av, *amap, plan, rows, c_dev, c_type, ldc, b->d_err,
+                           true, stream));
         b->launches++;
     } else {
         st = ensure_dev(reinterpret_cast<void **>(&b->d_y), &b->y_elems,
                         (size_t)rows * v.N * sizeof(float));
         if (st) return st;
-        QL_TRY(launch_gemm(v, w->wmap, av, *amap, plan, rows, b->d_y, kF32, v.N, b->d_err, stream));
+        QL_TRY(launch_gemm(v, w->wmap, av, *amap, plan, rows, b->d_y, kF32, v.N, b->d_err, true,
+                           stream));
         QL_TRY(launch_swiglu(b->d_y, rows, v.N, c_dev, c_type, ldc, stream));
         b->launches += 2;
     }
