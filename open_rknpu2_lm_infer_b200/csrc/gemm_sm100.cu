@@ -1,35 +1,41 @@
 // gemm_sm100.cu -- prefill path: int8 x (int4|int8) -> int32 on the 5th-generation tensor
-// core (tcgen05.mma kind::i8, accumulators in tensor memory), fed by TMA.
+// core (tcgen05.mma kind::i8, accumulators in tensor memory), fed by TMA, run by CTA pairs.
 //
 // Computes acc[m][n] = sum_k q[m][k] * w[k][n] exactly (src/npu.rs:1111-1116) and the
 // epilogue y = (f32(acc) * s_a[m]) * s_w[n] (src/npu.rs:1117) in registers.
 //
-// Orientation: the MMA's M dimension (128) is weight channels, its N dimension (`tok`,
-// 16..256) is tokens:  D[ch][tok] = W[ch][:] . X[tok][:].  One CTA tile is 256 channels x
-// tok tokens, computed as two M=128 MMAs that share every activation tile, which halves
-// the bytes each SM must pull per multiply-accumulate compared with a 128 x 256 tile (the
-// SM's ingress bandwidth, not the tensor core, bounds a 128-channel tile on B200).
+// Orientation: the MMA's M dimension is weight channels, its N dimension (`tok`, 32..256)
+// tokens:  D[ch][tok] = W[ch][:] . X[tok][:].  A cluster of two CTAs on the two SMs of a
+// TPC computes a 256-channel x tok tile with tcgen05.mma.cta_group::2 (M = 256): each CTA
+// stages its own 128 weight channels and half of the tok activation rows, the tensor core
+// reads both halves of B across the pair, and each CTA's tensor memory receives the
+// accumulators of its 128 channels for all tok tokens.  Measured on B200, a one-CTA M=128
+// MMA is bounded by the tensor core's shared-memory operand bandwidth (~2.9 POPS at
+// N=256); the pair halves each SM's operand traffic, and the 256-wide tile halves the
+// bytes each SM pulls from L2 per multiply-accumulate.
 //
-// Pipeline (one persistent CTA per SM; tiles strided over the grid, token tile fastest so
-// CTAs running side by side share a weight tile through L2); k-blocks are 64 deep and use
-// the 64-byte swizzle so the load ring is 6 stages deep:
-//   warp 0        TMA producer.  Per k-block: the activation tile [tok][64] (SW64) and
-//                 either the W8 weight tile [256][64] (SW64) or the packed W4 tile
-//                 [256][32 bytes].  Weight loads of the first stages are issued before
-//                 griddepcontrol.wait, so with programmatic dependent launch they overlap
-//                 the activation-quantisation kernel.
-//   warp 1        TMEM allocator and MMA issuer (one thread): 2 halves x 2 K-steps of
-//                 tcgen05.mma (M128 x N tok x K32) per k-block; tcgen05.commit releases the
-//                 smem slots and, per tile, hands the accumulators to the epilogue.
-//   warps 2..9    epilogue: warp (quadrant q, half h) drains TMEM lanes 32q.. of the half-h
-//                 accumulator with tcgen05.ld (32 lanes x 16 columns), dequantises and
-//                 stores.  When 4*tok <= 512 columns the accumulators are double-buffered
-//                 so the epilogue of one tile overlaps the main loop of the next.
-//   warps 10..13  (W4 only) converter: packed nibbles -> 8-bit codes in the SW64 K-major
-//                 layout of a separate 3-slot ring.  The nibbles stay offset-binary
-//                 (u = code + 8; A is declared unsigned) so the unpack is two masks per
-//                 word; the epilogue subtracts 8 * sum_k q[m][k].
-// Every mbarrier wait is bounded (common.cuh); on a timeout the CTA unwinds, drains its
+// Roles (one persistent CTA pair per TPC; tiles strided over the clusters, the token tile
+// fastest so neighbouring pairs share a weight tile through L2); 64-deep k-blocks in the
+// 64-byte swizzle, a ring of up to 16 stages:
+//   warp 0        TMA producer (both CTAs).  Activation half-tile [tok/2][64] and, for W8,
+//                 the weight tile [128][64], both counted on the leader CTA's `full`
+//                 barrier (cta_group::2 copies); for W4 the packed tile [128][32 bytes]
+//                 into this CTA's staging ring.  Weight loads of the first stages are issued
+//                 before griddepcontrol.wait, overlapping the activation-quantisation kernel
+//                 under programmatic dependent launch.
+//   warp 1        tensor-memory allocation (both CTAs, pair-wide); in the leader CTA one
+//                 thread issues 2 MMAs (K=32 each) per k-block and commits them to the
+//                 barriers of both CTAs (multicast commit), freeing the smem slots and, per
+//                 tile, handing the accumulators to the epilogues.
+//   warps 2..9    epilogue (both CTAs): warp (lane quadrant q, column half) drains its
+//                 part of the tensor-memory accumulator with tcgen05.ld, dequantises and
+//                 stores.  Accumulators are double-buffered (2 x tok <= 512 columns) so the
+//                 epilogue of one tile overlaps the main loop of the next.
+//   warps 10..13  (W4 only, both CTAs) converter: packed nibbles -> 8-bit codes in the
+//                 SW64 K-major layout of a separate 4-slot ring, announced to the leader.
+//                 The nibbles stay offset-binary (u = code + 8; A is declared unsigned) so
+//                 the unpack is two masks per word; the epilogue subtracts 8 * sum_k q[m][k].
+// Every mbarrier wait is bounded (common.cuh); on a timeout the pair unwinds, drains its
 // in-flight copies and MMAs and frees its tensor memory.
 #include "common.cuh"
 #include "kernels.h"
@@ -41,14 +47,16 @@ namespace ql {
 
 namespace {
 
-constexpr int KB = 64;                    // k-block depth (int8 codes per row per stage)
-constexpr int CHT = 2 * CH_TILE;          // 256 channels per CTA tile
-constexpr int A_SLOT = CHT * KB;          // 16 KB unpacked weights
-constexpr int P_SLOT = CHT * KB / 2;      // 8 KB packed W4
-constexpr int A_SLOTS_W4 = 3;             // converter ring depth
-constexpr int MAX_DYN_SMEM = 232448;      // 227 KB opt-in per block on sm_100
-constexpr int SMEM_RESERVE = 1024 + 512;  // alignment slack + barriers
-constexpr int MAX_STAGES = 8;
+constexpr int KB = GEMM_KB;                 // k-block depth (int8 codes per row per stage)
+constexpr int CH_CTA = CH_TILE;             // 128 channels per CTA
+constexpr int CHT = 2 * CH_CTA;             // 256 channels per pair tile
+constexpr int A_SLOT = CH_CTA * KB;         // 8 KB unpacked weights per CTA
+constexpr int P_SLOT = CH_CTA * KB / 2;     // 4 KB packed W4 per CTA
+constexpr int A_SLOTS = 4;                  // converter ring depth
+constexpr int EPI_WARPS = 8;
+constexpr int MAX_DYN_SMEM = 232448;        // 227 KB opt-in per block on sm_100
+constexpr int SMEM_RESERVE = 1024 + 1024;   // alignment slack + barriers
+constexpr int MAX_STAGES = 16;
 
 struct GemmArgs {
     const float *wscale;
@@ -57,15 +65,26 @@ struct GemmArgs {
     void *out;
     long long ldc;
     int M, N, nkb;
-    int tok, stages, n_tok_tiles, num_tiles, acc_bufs;
+    int tok, stages, n_tok_tiles, num_tiles;
     uint32_t tmem_cols;
     unsigned *err;
 };
 
 template <int BITS>
-constexpr int gemm_threads() { return BITS == 4 ? 448 : 320; }
+constexpr int gemm_threads() { return (2 + EPI_WARPS + (BITS == 4 ? 4 : 0)) * 32; }
 
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t cluster_id_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t num_clusters_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
 
 // Shared-memory descriptor, K-major, 64-byte swizzle: rows of 64 bytes, 8-row groups 512
 // bytes apart (stride byte offset), leading byte offset 16 (unused for swizzled K-major),
@@ -85,38 +104,41 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                                                 ~uintptr_t(1023));
     const int S = p.stages;
     const int tok = p.tok;
-    const int b_slot = tok * KB;
-    constexpr int w_slot = BITS == 8 ? A_SLOT : P_SLOT;   // what TMA brings per k-block
-    uint8_t *sB = smem;                                    // [S][tok][64]
-    uint8_t *sW = sB + S * b_slot;                         // [S][256][64] or [S][256][32]
-    uint8_t *sA = sW + S * w_slot;                         // W4: [3][256][64] unpacked
-    uint64_t *bars =
-        reinterpret_cast<uint64_t *>(sA + (BITS == 4 ? A_SLOTS_W4 * A_SLOT : 0));
-    uint64_t *full = bars;                  // [S]  TMA bytes landed
-    uint64_t *empty = full + S;             // [S]  slot consumed (MMA, and converter for W4)
-    uint64_t *afull = empty + S;            // [3]  W4: converter wrote A slot
-    uint64_t *aempty = afull + A_SLOTS_W4;  // [3]  W4: MMA done with A slot
-    uint64_t *accf = aempty + A_SLOTS_W4;   // [2]  accumulators ready for the epilogue
-    uint64_t *acce = accf + 2;              // [2]  epilogue drained the accumulators
-    uint64_t *drain = acce + 2;             // [1]  MMA drain on abort
+    const int b_half = (tok / 2) * KB;                    // this CTA's activation rows
+    constexpr int w_slot = BITS == 8 ? A_SLOT : P_SLOT;  // what TMA brings per k-block
+    uint8_t *sB = smem;                                   // [S][tok/2][64]
+    uint8_t *sW = sB + S * b_half;                        // [S][128][64] or [S][128][32]
+    uint8_t *sA = sW + S * w_slot;                        // W4: [4][128][64] unpacked
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sA + (BITS == 4 ? A_SLOTS * A_SLOT : 0));
+    uint64_t *full = bars;              // [S] leader: both CTAs' TMA bytes landed
+    uint64_t *empty = full + S;         // [S] slot consumed (MMA; W4 also the converter)
+    uint64_t *pfull = empty + S;        // [S] W4: this CTA's packed tile landed
+    uint64_t *afull = pfull + S;        // [4] leader: both converters wrote the A slot
+    uint64_t *aempty = afull + A_SLOTS; // [4] MMA done with the A slot
+    uint64_t *accf = aempty + A_SLOTS;  // [2] accumulators ready for the epilogue
+    uint64_t *acce = accf + 2;          // [2] leader: both epilogues drained them
+    uint64_t *drain = acce + 2;         // [1] leader: MMA drain on abort
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();  // 0 = leader
+    const uint32_t cid = cluster_id_x(), ncl = num_clusters_x();
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], BITS == 4 ? 1 + 128 : 1);
+            mbar_init(&pfull[s], 1);
         }
-        for (int a = 0; a < A_SLOTS_W4; a++) {
-            mbar_init(&afull[a], 128);
+        for (int a = 0; a < A_SLOTS; a++) {
+            mbar_init(&afull[a], 2 * 128);
             mbar_init(&aempty[a], 1);
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&accf[b], 1);
-            mbar_init(&acce[b], 256);
+            mbar_init(&acce[b], 2 * EPI_WARPS);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -127,124 +149,127 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
         tma_prefetch_desc(&amap);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, p.tmem_cols);
-        tmem_relinquish();
+        tmem_alloc_pair(tmem_slot, p.tmem_cols);
+        tmem_relinquish_pair();
     }
     tc_fence_before();
     __syncthreads();
+    cluster_sync();  // the peer's barriers are initialised before anyone signals them
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     unsigned *err = p.err;
-    const uint32_t tx_bytes = (uint32_t)(b_slot + w_slot);
+    const uint32_t full0 = map_to_rank(&full[0], 0);  // leader's barriers (cluster addresses)
+    const uint32_t afull0 = map_to_rank(&afull[0], 0);
+    const uint32_t acce0 = map_to_rank(&acce[0], 0);
+    // bytes the leader's `full` barrier receives per stage from both CTAs
+    const uint32_t tx_pair = 2u * (uint32_t)(b_half + (BITS == 8 ? A_SLOT : 0));
 
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
+            auto load_weights = [&](int s, int kb, int tc) {
+                if (BITS == 8) {
+                    tma_load_2d_pair(sW + s * w_slot, &wmap, full0 + 8u * s, kb * KB,
+                                     tc * CHT + (int)rank * CH_CTA);
+                } else {
+                    mbar_arrive_expect_tx(&pfull[s], P_SLOT);
+                    tma_load_2d(sW + s * w_slot, &wmap, &pfull[s], kb * (KB / 2),
+                                tc * CHT + (int)rank * CH_CTA);
+                }
+                if (rank == 0) mbar_arrive_expect_tx(&full[s], tx_pair);
+            };
             // Weight tiles of the first stages do not depend on the preceding kernel:
             // issue them before waiting for it.
-            const int pre = ((int)blockIdx.x < p.num_tiles) ? std::min(S, p.nkb) : 0;
-            {
-                const int tc = blockIdx.x / p.n_tok_tiles;
-                for (int j = 0; j < pre; j++) {
-                    mbar_arrive_expect_tx(&full[j], tx_bytes);
-                    tma_load_2d(sW + j * w_slot, &wmap, &full[j], j * (BITS == 8 ? KB : KB / 2),
-                                tc * CHT);
-                }
-            }
+            const int pre = ((int)cid < p.num_tiles) ? std::min(S, p.nkb) : 0;
+            for (int j = 0; j < pre; j++) load_weights(j, j, (int)cid / p.n_tok_tiles);
             grid_dep_wait();
             uint32_t it = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+            for (int t = (int)cid; t < p.num_tiles && ok; t += (int)ncl) {
                 const int tc = t / p.n_tok_tiles, tt = t % p.n_tok_tiles;
                 for (int kb = 0; kb < p.nkb; kb++, it++) {
                     const int s = it % S;
-                    const uint32_t ph = (it / S) & 1;
                     if (it >= (uint32_t)pre) {
-                        if (!(ok = mbar_wait(&empty[s], ph ^ 1, err, abort_flag))) break;
-                        mbar_arrive_expect_tx(&full[s], tx_bytes);
-                        tma_load_2d(sW + s * w_slot, &wmap, &full[s],
-                                    kb * (BITS == 8 ? KB : KB / 2), tc * CHT);
+                        if (!(ok = mbar_wait(&empty[s], ((it / S) & 1) ^ 1, err, abort_flag))) break;
+                        load_weights(s, kb, tc);
                     }
-                    tma_load_2d(sB + s * b_slot, &amap, &full[s], kb * KB, tt * tok);
+                    tma_load_2d_pair(sB + s * b_half, &amap, full0 + 8u * s, kb * KB,
+                                     tt * tok + (int)rank * (tok / 2));
                 }
             }
             if (!ok) {
-                // Let every copy already issued land before the CTA exits.
+                // Let the copies already issued land before the pair exits.
                 volatile int never = 0;
                 const uint32_t issued = std::max(it, (uint32_t)pre);
                 const uint32_t first = issued > (uint32_t)S ? issued - S : 0;
-                for (uint32_t j = first; j < issued; j++)
-                    mbar_wait(&full[j % S], (j / S) & 1, nullptr, &never);
+                for (uint32_t j = first; j < issued; j++) {
+                    if (rank == 0) mbar_wait(&full[j % S], (j / S) & 1, nullptr, &never);
+                    if (BITS == 4) mbar_wait(&pfull[j % S], (j / S) & 1, nullptr, &never);
+                }
             }
         }
     } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            const uint32_t idesc = idesc_i8(CH_TILE, tok, BITS == 8, true);
+        // ------------------------------------------------------------ MMA issuer (leader)
+        if (lane == 0 && rank == 0) {
+            const uint32_t idesc = idesc_i8(2 * CH_CTA, tok, BITS == 8, true);
             uint32_t it = 0, local = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, local++) {
-                const int ab = local % p.acc_bufs;
-                const uint32_t aph = (local / p.acc_bufs) & 1;
-                if (!(ok = mbar_wait(&acce[ab], aph ^ 1, err, abort_flag))) break;
+            for (int t = (int)cid; t < p.num_tiles && ok; t += (int)ncl, local++) {
+                const int ab = local & 1;
+                if (!(ok = mbar_wait(&acce[ab], ((local >> 1) & 1) ^ 1, err, abort_flag))) break;
                 tc_fence_after();
-                const uint32_t d0 = tmem_base + (uint32_t)(ab * 2 * tok);
+                const uint32_t d = tmem_base + (uint32_t)(ab * tok);
                 for (int kb = 0; kb < p.nkb; kb++, it++) {
                     const int s = it % S;
-                    const uint32_t ph = (it / S) & 1;
-                    const int a = it % A_SLOTS_W4;
-                    if (!(ok = mbar_wait(&full[s], ph, err, abort_flag))) break;
+                    const int a = it % A_SLOTS;
+                    if (!(ok = mbar_wait(&full[s], (it / S) & 1, err, abort_flag))) break;
                     if (BITS == 4 &&
-                        !(ok = mbar_wait(&afull[a], (it / A_SLOTS_W4) & 1, err, abort_flag)))
+                        !(ok = mbar_wait(&afull[a], (it / A_SLOTS) & 1, err, abort_flag)))
                         break;
                     tc_fence_after();
-                    const uint8_t *At = BITS == 8 ? sW + s * w_slot : sA + a * A_SLOT;
-                    const uint64_t bdesc = smem_desc_sw64(sB + s * b_slot);
+                    const uint64_t adesc =
+                        smem_desc_sw64(BITS == 8 ? sW + s * w_slot : sA + a * A_SLOT);
+                    const uint64_t bdesc = smem_desc_sw64(sB + s * b_half);
 #pragma unroll
-                    for (int h = 0; h < 2; h++) {
-                        const uint64_t adesc = smem_desc_sw64(At + h * (CH_TILE * KB));
-#pragma unroll
-                        for (int k = 0; k < KB / 32; k++)
-                            mma_i8_ss(d0 + (uint32_t)(h * tok), adesc + 2 * k, bdesc + 2 * k,
-                                      idesc, (kb | k) != 0);
-                    }
-                    mma_commit(&empty[s]);
-                    if (BITS == 4) mma_commit(&aempty[a]);
+                    for (int k = 0; k < KB / 32; k++)
+                        mma_i8_ss_pair(d, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+                    mma_commit_pair(&empty[s], 0x3);
+                    if (BITS == 4) mma_commit_pair(&aempty[a], 0x3);
                 }
-                if (ok) mma_commit(&accf[ab]);
+                if (ok) mma_commit_pair(&accf[ab], 0x3);
             }
             if (!ok) {
                 volatile int never = 0;
-                mma_commit(drain);
+                mma_commit_pair(drain, 0x1);  // leader's drain barrier only
                 mbar_wait(drain, 0, nullptr, &never);
             }
         }
-    } else if (warp < 10) {
+    } else if (warp < 2 + EPI_WARPS) {
         // ------------------------------------------------------------ epilogue
-        grid_dep_wait();  // the activation scales/rowsums come from the previous kernel
-        const int q = warp & 3;            // TMEM lane quadrant this warp may access
-        const int h = (warp - 2) >> 2;     // accumulator half (channels h*128 ..)
+        grid_dep_wait();  // the activation scales / row sums come from the previous kernel
+        const int q = warp & 3;                 // TMEM lane quadrant this warp may access
+        const int colh = (warp - 2) >> 2;       // which half of the tok columns
+        const int cols = tok / 2;
         uint32_t local = 0;
         OutT *out = static_cast<OutT *>(p.out);
-        for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, local++) {
+        for (int t = (int)cid; t < p.num_tiles; t += (int)ncl, local++) {
             const int tc = t / p.n_tok_tiles, tt = t % p.n_tok_tiles;
-            const int ab = local % p.acc_bufs;
-            const uint32_t aph = (local / p.acc_bufs) & 1;
+            const int ab = local & 1;
             // every lane waits (bounded); the warp leaves together if any lane gave up,
             // so the warp-collective tcgen05.ld / shuffles below stay converged
-            const bool okw = mbar_wait(&accf[ab], aph, err, abort_flag);
+            const bool okw = mbar_wait(&accf[ab], (local >> 1) & 1, err, abort_flag);
             if (!__all_sync(0xffffffffu, okw)) break;
             tc_fence_after();
-            const int ch = tc * CHT + h * CH_TILE + q * 32 + lane;
+            const int ch = tc * CHT + (int)rank * CH_CTA + q * 32 + lane;
             const bool chv = ch < p.N;
             const float sw = chv ? p.wscale[ch] : 0.0f;
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) +
-                                   (uint32_t)(ab * 2 * tok + h * tok);
-            for (int c = 0; c < tok / 16; c++) {
+                                   (uint32_t)(ab * tok + colh * cols);
+            for (int c = 0; c < cols / 16; c++) {
                 uint32_t r[16];
                 tmem_ld16(taddr + c * 16, r);
                 tmem_ld_wait();
-                const int tok0 = tt * tok + c * 16;
+                const int tok0 = tt * tok + colh * cols + c * 16;
                 const bool lv = lane < 16 && tok0 + lane < p.M;
                 const float sa_l = lv ? p.ascale[tok0 + lane] : 0.0f;
                 const int rs_l = (BITS == 4 && lv) ? p.rowsum[tok0 + lane] : 0;
@@ -266,28 +291,29 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                 }
             }
             tc_fence_before();
-            mbar_arrive(&acce[ab]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(acce0 + 8u * ab);
         }
     } else {
         // ------------------------------------------------------------ W4 converter
         if constexpr (BITS == 4) {
-            const int ct = threadIdx.x - 320;  // 0..127
-            const int half = ct & 1;           // which 16-byte half of a 32-byte packed row
+            const int ct = threadIdx.x - (2 + EPI_WARPS) * 32;  // 0..127
             uint32_t it = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+            for (int t = (int)cid; t < p.num_tiles && ok; t += (int)ncl) {
                 for (int kb = 0; kb < p.nkb; kb++, it++) {
                     const int s = it % S;
-                    const int a = it % A_SLOTS_W4;
-                    if (!(ok = mbar_wait(&full[s], (it / S) & 1, err, abort_flag))) break;
-                    if (!(ok = mbar_wait(&aempty[a], ((it / A_SLOTS_W4) & 1) ^ 1, err, abort_flag)))
+                    const int a = it % A_SLOTS;
+                    if (!(ok = mbar_wait(&pfull[s], (it / S) & 1, err, abort_flag))) break;
+                    if (!(ok = mbar_wait(&aempty[a], ((it / A_SLOTS) & 1) ^ 1, err, abort_flag)))
                         break;
                     const uint8_t *P = sW + s * w_slot;
                     uint8_t *A = sA + a * A_SLOT;
 #pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        // a thread pair per row; 64 rows per pass
-                        const int row = (ct >> 1) + 64 * j;
+                    for (int j = 0; j < 2; j++) {
+                        // two threads per row (one 16-byte half of the 32 packed bytes each)
+                        const int item = ct + 128 * j;
+                        const int row = item >> 1, half = item & 1;
                         const uint4 v = *reinterpret_cast<const uint4 *>(P + row * 32 + half * 16);
                         // 16 packed bytes = codes k = 32*half .. 32*half+31 of this k-block:
                         // word p covers 8 codes, low nibbles k 8p..8p+3, high 8p+4..8p+7.
@@ -300,7 +326,7 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                         *reinterpret_cast<uint4 *>(A + row * 64 + (((2 * half + 1) ^ sw) << 4)) = c1;
                     }
                     fence_proxy_async_smem();
-                    mbar_arrive(&afull[a]);
+                    mbar_arrive_remote(afull0 + 8u * a);
                     mbar_arrive(&empty[s]);
                 }
             }
@@ -309,9 +335,10 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
 
     tc_fence_before();
     __syncthreads();
+    cluster_sync();  // neither CTA leaves while the pair may still touch its shared memory
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, p.tmem_cols);
+        tmem_dealloc_pair(tmem_base, p.tmem_cols);
     }
 }
 
@@ -336,11 +363,15 @@ cudaError_t launch_t(const CUtensorMap &wmap, const CUtensorMap &amap, const Gem
     cfg.blockDim = dim3(gemm_threads<BITS>());
     cfg.dynamicSmemBytes = plan.smem_bytes;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, kern, wmap, amap, args);
 }
 
@@ -350,17 +381,17 @@ GemmPlan plan_gemm(const WeightView &w, int rows, int num_sms) {
     GemmPlan plan{};
     const int tiles_m = std::max(1, (rows + 255) / 256);
     int tok = (rows + tiles_m - 1) / tiles_m;
-    tok = std::max(16, (tok + 15) / 16 * 16);
+    tok = std::max(32, (tok + 31) / 32 * 32);  // 2-CTA MMA: N multiple of 32
     plan.tok = tok;
-    const int stage_bytes = tok * KB + (w.bits == 8 ? A_SLOT : P_SLOT);
-    const int fixed = SMEM_RESERVE + (w.bits == 4 ? A_SLOTS_W4 * A_SLOT : 0);
+    const int stage_bytes = (tok / 2) * KB + (w.bits == 8 ? A_SLOT : P_SLOT);
+    const int fixed = SMEM_RESERVE + (w.bits == 4 ? A_SLOTS * A_SLOT : 0);
     const int stages = std::min(MAX_STAGES, (MAX_DYN_SMEM - fixed) / stage_bytes);
     plan.stages = stages;
-    // One CTA per SM: the kernel allocates up to 512 TMEM columns.
+    // One CTA per SM: each CTA of the pair allocates up to 512 TMEM columns.
     plan.smem_bytes = std::max(stages * stage_bytes + fixed, 120 * 1024);
     const int n_tok_tiles = (rows + tok - 1) / tok;
     plan.tiles = ((w.Np + CHT - 1) / CHT) * n_tok_tiles;
-    plan.grid = std::min(plan.tiles, num_sms);
+    plan.grid = 2 * std::min(plan.tiles, num_sms / 2);
     return plan;
 }
 
@@ -381,9 +412,8 @@ cudaError_t launch_gemm(const WeightView &w, const CUtensorMap &wmap, const ActV
     args.stages = plan.stages;
     args.n_tok_tiles = (rows + plan.tok - 1) / plan.tok;
     args.num_tiles = plan.tiles;
-    args.acc_bufs = (4 * plan.tok <= 512) ? 2 : 1;
     uint32_t cols = 32;
-    while (cols < (uint32_t)(2 * plan.tok * args.acc_bufs)) cols <<= 1;
+    while (cols < (uint32_t)(2 * plan.tok)) cols <<= 1;
     args.tmem_cols = cols;
     args.err = err;
     if (w.bits == 8) {

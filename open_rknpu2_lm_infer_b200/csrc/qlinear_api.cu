@@ -145,17 +145,17 @@ bool tma_available() {
     load_encode();
     return g_encode != nullptr;
 }
-// The GEMM streams 64-deep k-blocks of 256-channel weight tiles (64-byte swizzle for the
-// 8-bit operands; packed W4 rows of 32 bytes are unpacked by the kernel itself).
+// The GEMM runs on CTA pairs: each CTA streams 64-deep k-blocks of its 128 weight channels
+// (64-byte swizzle for 8-bit operands; packed W4 rows of 32 bytes, unpacked in the kernel)
+// and of half of the token tile.
 bool encode_weight_map(const WeightView &w, CUtensorMap *map) {
     if (w.bits == 8)
-        return encode_2d(map, w.w, w.Kp, w.Np, w.Kp, GEMM_KB, 2 * CH_TILE,
-                         CU_TENSOR_MAP_SWIZZLE_64B);
-    return encode_2d(map, w.w, w.Kp / 2, w.Np, w.Kp / 2, GEMM_KB / 2, 2 * CH_TILE,
+        return encode_2d(map, w.w, w.Kp, w.Np, w.Kp, GEMM_KB, CH_TILE, CU_TENSOR_MAP_SWIZZLE_64B);
+    return encode_2d(map, w.w, w.Kp / 2, w.Np, w.Kp / 2, GEMM_KB / 2, CH_TILE,
                      CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 bool encode_act_map(const int8_t *codes, int rows_cap, int Kp, int tok, CUtensorMap *map) {
-    return encode_2d(map, codes, Kp, rows_cap, Kp, GEMM_KB, tok, CU_TENSOR_MAP_SWIZZLE_64B);
+    return encode_2d(map, codes, Kp, rows_cap, Kp, GEMM_KB, tok / 2, CU_TENSOR_MAP_SWIZZLE_64B);
 }
 }  // namespace ql
 
