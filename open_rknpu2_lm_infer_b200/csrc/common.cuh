@@ -27,7 +27,7 @@ constexpr unsigned long long QL_WAIT_NS = 2000000000ull;  // 2 s per wait
 // GEMM geometry shared by the weight packer and the kernels.
 constexpr int KBLK = 128;       // k-block: one 128-byte swizzle atom of int8 codes
 constexpr int CH_TILE = 128;    // weight channels per MMA (the MMA's M)
-constexpr int GEMM_KB = 64;     // k-block depth of the tensor-core GEMM's TMA tiles
+constexpr int GEMM_KB = 128;    // k-block depth of the tensor-core GEMM's TMA tiles
 
 __host__ __device__ inline long long round_up(long long v, long long m) { return (v + m - 1) / m * m; }
 

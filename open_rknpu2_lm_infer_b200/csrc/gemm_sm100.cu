@@ -15,16 +15,18 @@
 // bytes each SM pulls from L2 per multiply-accumulate.
 //
 // Roles (one persistent CTA pair per TPC; tiles strided over the clusters, the token tile
-// fastest so neighbouring pairs share a weight tile through L2); 64-deep k-blocks in the
-// 64-byte swizzle, a ring of up to 16 stages:
-//   warp 0        TMA producer (both CTAs).  Activation half-tile [tok/2][64] and, for W8,
-//                 the weight tile [128][64], both counted on the leader CTA's `full`
-//                 barrier (cta_group::2 copies); for W4 the packed tile [128][32 bytes]
+// fastest so neighbouring pairs share a weight tile through L2); 128-deep k-blocks in the
+// 128-byte swizzle (4 MMAs per hand-off: measured on B200, one producer -> MMA -> commit
+// round costs ~400 cycles, so a hand-off must carry at least that much tensor work), a ring
+// of up to 8 stages:
+//   warp 0        TMA producer (both CTAs).  Activation half-tile [tok/2][128] and, for W8,
+//                 the weight tile [128][128], both counted on the leader CTA's `full`
+//                 barrier (cta_group::2 copies); for W4 the packed tile [128][64 bytes]
 //                 into this CTA's staging ring.  Weight loads of the first stages are issued
 //                 before griddepcontrol.wait, overlapping the activation-quantisation kernel
 //                 under programmatic dependent launch.
 //   warp 1        tensor-memory allocation (both CTAs, pair-wide); in the leader CTA one
-//                 thread issues 2 MMAs (K=32 each) per k-block and commits them to the
+//                 thread issues 4 MMAs (K=32 each) per k-block and commits them to the
 //                 barriers of both CTAs (multicast commit), freeing the smem slots and, per
 //                 tile, handing the accumulators to the epilogues.
 //   warps 2..9    epilogue (both CTAs): warp (lane quadrant q, column half) drains its
@@ -32,7 +34,7 @@
 //                 stores.  Accumulators are double-buffered (2 x tok <= 512 columns) so the
 //                 epilogue of one tile overlaps the main loop of the next.
 //   warps 10..13  (W4 only, both CTAs) converter: packed nibbles -> 8-bit codes in the
-//                 SW64 K-major layout of a separate 4-slot ring, announced to the leader.
+//                 SW128 K-major layout of a separate 3-slot ring, announced to the leader.
 //                 The nibbles stay offset-binary (u = code + 8; A is declared unsigned) so
 //                 the unpack is two masks per word; the epilogue subtracts 8 * sum_k q[m][k].
 // Every mbarrier wait is bounded (common.cuh); on a timeout the pair unwinds, drains its
@@ -48,15 +50,16 @@ namespace ql {
 namespace {
 
 constexpr int KB = GEMM_KB;                 // k-block depth (int8 codes per row per stage)
+static_assert(KB == 128, "one 128-byte swizzle atom per row per stage");
 constexpr int CH_CTA = CH_TILE;             // 128 channels per CTA
 constexpr int CHT = 2 * CH_CTA;             // 256 channels per pair tile
-constexpr int A_SLOT = CH_CTA * KB;         // 8 KB unpacked weights per CTA
-constexpr int P_SLOT = CH_CTA * KB / 2;     // 4 KB packed W4 per CTA
-constexpr int A_SLOTS = 4;                  // converter ring depth
+constexpr int A_SLOT = CH_CTA * KB;         // 16 KB unpacked weights per CTA
+constexpr int P_SLOT = CH_CTA * KB / 2;     // 8 KB packed W4 per CTA
+constexpr int A_SLOTS = 3;                  // converter ring depth
 constexpr int EPI_WARPS = 8;
 constexpr int MAX_DYN_SMEM = 232448;        // 227 KB opt-in per block on sm_100
 constexpr int SMEM_RESERVE = 1024 + 1024;   // alignment slack + barriers
-constexpr int MAX_STAGES = 16;
+constexpr int MAX_STAGES = 8;
 
 struct GemmArgs {
     const float *wscale;
@@ -86,13 +89,14 @@ __device__ __forceinline__ uint32_t num_clusters_x() {
     return r;
 }
 
-// Shared-memory descriptor, K-major, 64-byte swizzle: rows of 64 bytes, 8-row groups 512
+// Shared-memory descriptor, K-major, 128-byte swizzle: rows of 128 bytes, 8-row groups 1024
 // bytes apart (stride byte offset), leading byte offset 16 (unused for swizzled K-major),
-// version 1, layout type 4 (SWIZZLE_64B).
-__device__ __forceinline__ uint64_t smem_desc_sw64(const void *tile) {
+// version 1, layout type 2 (SWIZZLE_128B).  Advancing the start address by 32 bytes steps
+// one MMA (K = 32) along the row; the swizzle is applied to absolute address bits.
+__device__ __forceinline__ uint64_t smem_desc_sw128_k(const void *tile) {
     const uint64_t addr = smem_u32(tile);
-    return ((addr >> 4) & 0x3FFFull) | ((uint64_t)1 << 16) | ((uint64_t)(512 >> 4) << 32) |
-           ((uint64_t)1 << 46) | ((uint64_t)4 << 61);
+    return ((addr >> 4) & 0x3FFFull) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
 template <int BITS, typename OutT>
@@ -106,15 +110,15 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
     const int tok = p.tok;
     const int b_half = (tok / 2) * KB;                    // this CTA's activation rows
     constexpr int w_slot = BITS == 8 ? A_SLOT : P_SLOT;  // what TMA brings per k-block
-    uint8_t *sB = smem;                                   // [S][tok/2][64]
-    uint8_t *sW = sB + S * b_half;                        // [S][128][64] or [S][128][32]
-    uint8_t *sA = sW + S * w_slot;                        // W4: [4][128][64] unpacked
+    uint8_t *sB = smem;                                   // [S][tok/2][128]
+    uint8_t *sW = sB + S * b_half;                        // [S][128][128] or [S][128][64]
+    uint8_t *sA = sW + S * w_slot;                        // W4: [3][128][128] unpacked
     uint64_t *bars = reinterpret_cast<uint64_t *>(sA + (BITS == 4 ? A_SLOTS * A_SLOT : 0));
     uint64_t *full = bars;              // [S] leader: both CTAs' TMA bytes landed
     uint64_t *empty = full + S;         // [S] slot consumed (MMA; W4 also the converter)
     uint64_t *pfull = empty + S;        // [S] W4: this CTA's packed tile landed
-    uint64_t *afull = pfull + S;        // [4] leader: both converters wrote the A slot
-    uint64_t *aempty = afull + A_SLOTS; // [4] MMA done with the A slot
+    uint64_t *afull = pfull + S;        // [3] leader: both converters wrote the A slot
+    uint64_t *aempty = afull + A_SLOTS; // [3] MMA done with the A slot
     uint64_t *accf = aempty + A_SLOTS;  // [2] accumulators ready for the epilogue
     uint64_t *acce = accf + 2;          // [2] leader: both epilogues drained them
     uint64_t *drain = acce + 2;         // [1] leader: MMA drain on abort
@@ -129,11 +133,11 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], BITS == 4 ? 1 + 128 : 1);
+            mbar_init(&empty[s], BITS == 4 ? 2 : 1);
             mbar_init(&pfull[s], 1);
         }
         for (int a = 0; a < A_SLOTS; a++) {
-            mbar_init(&afull[a], 2 * 128);
+            mbar_init(&afull[a], 2);
             mbar_init(&aempty[a], 1);
         }
         for (int b = 0; b < 2; b++) {
@@ -183,18 +187,18 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
             const int pre = ((int)cid < p.num_tiles) ? std::min(S, p.nkb) : 0;
             for (int j = 0; j < pre; j++) load_weights(j, j, (int)cid / p.n_tok_tiles);
             grid_dep_wait();
-            uint32_t it = 0;
+            uint32_t it = 0, s = 0, ph = 0;  // iteration, stage, stage phase
             bool ok = true;
             for (int t = (int)cid; t < p.num_tiles && ok; t += (int)ncl) {
                 const int tc = t / p.n_tok_tiles, tt = t % p.n_tok_tiles;
                 for (int kb = 0; kb < p.nkb; kb++, it++) {
-                    const int s = it % S;
                     if (it >= (uint32_t)pre) {
-                        if (!(ok = mbar_wait(&empty[s], ((it / S) & 1) ^ 1, err, abort_flag))) break;
+                        if (!(ok = mbar_wait(&empty[s], ph ^ 1, err, abort_flag))) break;
                         load_weights(s, kb, tc);
                     }
                     tma_load_2d_pair(sB + s * b_half, &amap, full0 + 8u * s, kb * KB,
                                      tt * tok + (int)rank * (tok / 2));
+                    if (++s == (uint32_t)S) { s = 0; ph ^= 1; }
                 }
             }
             if (!ok) {
@@ -212,29 +216,29 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
         // ------------------------------------------------------------ MMA issuer (leader)
         if (lane == 0 && rank == 0) {
             const uint32_t idesc = idesc_i8(2 * CH_CTA, tok, BITS == 8, true);
-            uint32_t it = 0, local = 0;
+            uint32_t s = 0, ph = 0, a = 0, aph = 0, local = 0;
             bool ok = true;
             for (int t = (int)cid; t < p.num_tiles && ok; t += (int)ncl, local++) {
                 const int ab = local & 1;
                 if (!(ok = mbar_wait(&acce[ab], ((local >> 1) & 1) ^ 1, err, abort_flag))) break;
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(ab * tok);
-                for (int kb = 0; kb < p.nkb; kb++, it++) {
-                    const int s = it % S;
-                    const int a = it % A_SLOTS;
-                    if (!(ok = mbar_wait(&full[s], (it / S) & 1, err, abort_flag))) break;
-                    if (BITS == 4 &&
-                        !(ok = mbar_wait(&afull[a], (it / A_SLOTS) & 1, err, abort_flag)))
-                        break;
+                for (int kb = 0; kb < p.nkb; kb++) {
+                    if (!(ok = mbar_wait(&full[s], ph, err, abort_flag))) break;
+                    if (BITS == 4 && !(ok = mbar_wait(&afull[a], aph, err, abort_flag))) break;
                     tc_fence_after();
                     const uint64_t adesc =
-                        smem_desc_sw64(BITS == 8 ? sW + s * w_slot : sA + a * A_SLOT);
-                    const uint64_t bdesc = smem_desc_sw64(sB + s * b_half);
+                        smem_desc_sw128_k(BITS == 8 ? sW + s * w_slot : sA + a * A_SLOT);
+                    const uint64_t bdesc = smem_desc_sw128_k(sB + s * b_half);
 #pragma unroll
                     for (int k = 0; k < KB / 32; k++)
                         mma_i8_ss_pair(d, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
                     mma_commit_pair(&empty[s], 0x3);
-                    if (BITS == 4) mma_commit_pair(&aempty[a], 0x3);
+                    if (BITS == 4) {
+                        mma_commit_pair(&aempty[a], 0x3);
+                        if (++a == (uint32_t)A_SLOTS) { a = 0; aph ^= 1; }
+                    }
+                    if (++s == (uint32_t)S) { s = 0; ph ^= 1; }
                 }
                 if (ok) mma_commit_pair(&accf[ab], 0x3);
             }
@@ -298,36 +302,40 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
         // ------------------------------------------------------------ W4 converter
         if constexpr (BITS == 4) {
             const int ct = threadIdx.x - (2 + EPI_WARPS) * 32;  // 0..127
-            uint32_t it = 0;
+            const int cp = ct & 3;  // 16-byte chunk of a 64-byte packed row (32 codes)
+            uint32_t s = 0, ph = 0, a = 0, aph = 0;
             bool ok = true;
             for (int t = (int)cid; t < p.num_tiles && ok; t += (int)ncl) {
-                for (int kb = 0; kb < p.nkb; kb++, it++) {
-                    const int s = it % S;
-                    const int a = it % A_SLOTS;
-                    if (!(ok = mbar_wait(&pfull[s], (it / S) & 1, err, abort_flag))) break;
-                    if (!(ok = mbar_wait(&aempty[a], ((it / A_SLOTS) & 1) ^ 1, err, abort_flag)))
-                        break;
+                for (int kb = 0; kb < p.nkb; kb++) {
+                    if (!(ok = mbar_wait(&pfull[s], ph, err, abort_flag))) break;
+                    if (!(ok = mbar_wait(&aempty[a], aph ^ 1, err, abort_flag))) break;
                     const uint8_t *P = sW + s * w_slot;
                     uint8_t *A = sA + a * A_SLOT;
 #pragma unroll
-                    for (int j = 0; j < 2; j++) {
-                        // two threads per row (one 16-byte half of the 32 packed bytes each)
-                        const int item = ct + 128 * j;
-                        const int row = item >> 1, half = item & 1;
-                        const uint4 v = *reinterpret_cast<const uint4 *>(P + row * 32 + half * 16);
-                        // 16 packed bytes = codes k = 32*half .. 32*half+31 of this k-block:
+                    for (int j = 0; j < 4; j++) {
+                        // four threads per row (one 16-byte quarter of the 64 packed bytes each)
+                        const int row = (ct >> 2) + 32 * j;
+                        const uint4 v = *reinterpret_cast<const uint4 *>(P + row * 64 + cp * 16);
+                        // 16 packed bytes = codes k = 32*cp .. 32*cp+31 of this k-block:
                         // word p covers 8 codes, low nibbles k 8p..8p+3, high 8p+4..8p+7.
                         const uint4 c0 = make_uint4(v.x & 0x0F0F0F0Fu, (v.x >> 4) & 0x0F0F0F0Fu,
                                                     v.y & 0x0F0F0F0Fu, (v.y >> 4) & 0x0F0F0F0Fu);
                         const uint4 c1 = make_uint4(v.z & 0x0F0F0F0Fu, (v.z >> 4) & 0x0F0F0F0Fu,
                                                     v.w & 0x0F0F0F0Fu, (v.w >> 4) & 0x0F0F0F0Fu);
-                        const int sw = (row >> 1) & 3;  // 64-byte swizzle of this row
-                        *reinterpret_cast<uint4 *>(A + row * 64 + (((2 * half) ^ sw) << 4)) = c0;
-                        *reinterpret_cast<uint4 *>(A + row * 64 + (((2 * half + 1) ^ sw) << 4)) = c1;
+                        const int sw = row & 7;  // 128-byte swizzle of this row
+                        *reinterpret_cast<uint4 *>(A + row * 128 + (((2 * cp) ^ sw) << 4)) = c0;
+                        *reinterpret_cast<uint4 *>(A + row * 128 + (((2 * cp + 1) ^ sw) << 4)) = c1;
                     }
+                    // every writer makes its stores visible to the async proxy, the four
+                    // converter warps meet, then one thread announces the slot to the leader
                     fence_proxy_async_smem();
-                    mbar_arrive_remote(afull0 + 8u * a);
-                    mbar_arrive(&empty[s]);
+                    asm volatile("bar.sync 1, 128;" ::: "memory");
+                    if (ct == 0) {
+                        mbar_arrive_remote(afull0 + 8u * a);
+                        mbar_arrive(&empty[s]);
+                    }
+                    if (++a == (uint32_t)A_SLOTS) { a = 0; aph ^= 1; }
+                    if (++s == (uint32_t)S) { s = 0; ph ^= 1; }
                 }
             }
         }
@@ -360,6 +368,7 @@ cudaError_t launch_t(const CUtensorMap &wmap, const CUtensorMap &amap, const Gem
     }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(plan.grid);
+
     cfg.blockDim = dim3(gemm_threads<BITS>());
     cfg.dynamicSmemBytes = plan.smem_bytes;
     cfg.stream = stream;
@@ -375,9 +384,35 @@ cudaError_t launch_t(const CUtensorMap &wmap, const CUtensorMap &amap, const Gem
     return cudaLaunchKernelEx(&cfg, kern, wmap, amap, args);
 }
 
+template <int BITS>
+int pair_capacity_t() {
+    cudaLaunchConfig_t q{};
+    q.gridDim = dim3(2);
+    q.blockDim = dim3(gemm_threads<BITS>());
+    q.dynamicSmemBytes = MAX_DYN_SMEM - 1024;
+    cudaLaunchAttribute qa[1];
+    qa[0].id = cudaLaunchAttributeClusterDimension;
+    qa[0].val.clusterDim.x = 2;
+    qa[0].val.clusterDim.y = 1;
+    qa[0].val.clusterDim.z = 1;
+    q.attrs = qa;
+    q.numAttrs = 1;
+    auto kern = gemm_kernel<BITS, __half>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_DYN_SMEM) !=
+        cudaSuccess)
+        return 0;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &q) != cudaSuccess) return 0;
+    return n;
+}
+
 }  // namespace
 
-GemmPlan plan_gemm(const WeightView &w, int rows, int num_sms) {
+// How many CTA pairs of the GEMM the current device holds at once (TPCs whose two SMs are
+// both available); the persistent grid is sized to it so every pair is resident.
+int gemm_pair_capacity(int bits) { return bits == 8 ? pair_capacity_t<8>() : pair_capacity_t<4>(); }
+
+GemmPlan plan_gemm(const WeightView &w, int rows, int max_pairs) {
     GemmPlan plan{};
     const int tiles_m = std::max(1, (rows + 255) / 256);
     int tok = (rows + tiles_m - 1) / tiles_m;
@@ -391,7 +426,7 @@ GemmPlan plan_gemm(const WeightView &w, int rows, int num_sms) {
     plan.smem_bytes = std::max(stages * stage_bytes + fixed, 120 * 1024);
     const int n_tok_tiles = (rows + tok - 1) / tok;
     plan.tiles = ((w.Np + CHT - 1) / CHT) * n_tok_tiles;
-    plan.grid = 2 * std::min(plan.tiles, num_sms / 2);
+    plan.grid = 2 * std::min(plan.tiles, std::max(1, max_pairs));
     return plan;
 }
 

@@ -52,7 +52,9 @@ struct GemmPlan {
     int grid;       // persistent CTAs
     int tiles;
 };
-GemmPlan plan_gemm(const WeightView &w, int rows, int num_sms);
+// max_pairs: gemm_pair_capacity() of the device (CTA pairs resident at once).
+GemmPlan plan_gemm(const WeightView &w, int rows, int max_pairs);
+int gemm_pair_capacity(int bits);
 // pdl: launch with programmatic stream serialization (the kernel waits with
 // griddepcontrol.wait before reading the activation codes / scales).
 cudaError_t launch_gemm(const WeightView &w, const CUtensorMap &wmap, const ActView &a,

@@ -32,6 +32,7 @@ struct qlinear_backend {
     int device = 0;
     int round_mode = QLINEAR_ROUND_AWAY;
     int num_sms = 148;
+    int gemm_pairs[2] = {0, 0};  // resident CTA pairs of the W4 / W8 GEMM
     cudaStream_t stream = nullptr;  // host-path calls and uploads
     unsigned *d_err = nullptr;
     unsigned *h_err = nullptr;      // pinned
@@ -145,17 +146,17 @@ bool tma_available() {
     load_encode();
     return g_encode != nullptr;
 }
-// The GEMM runs on CTA pairs: each CTA streams 64-deep k-blocks of its 128 weight channels
-// (64-byte swizzle for 8-bit operands; packed W4 rows of 32 bytes, unpacked in the kernel)
+// The GEMM runs on CTA pairs: each CTA streams 128-deep k-blocks of its 128 weight channels
+// (128-byte swizzle for 8-bit operands; packed W4 rows of 64 bytes, unpacked in the kernel)
 // and of half of the token tile.
 bool encode_weight_map(const WeightView &w, CUtensorMap *map) {
     if (w.bits == 8)
-        return encode_2d(map, w.w, w.Kp, w.Np, w.Kp, GEMM_KB, CH_TILE, CU_TENSOR_MAP_SWIZZLE_64B);
+        return encode_2d(map, w.w, w.Kp, w.Np, w.Kp, GEMM_KB, CH_TILE, CU_TENSOR_MAP_SWIZZLE_128B);
     return encode_2d(map, w.w, w.Kp / 2, w.Np, w.Kp / 2, GEMM_KB / 2, CH_TILE,
                      CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 bool encode_act_map(const int8_t *codes, int rows_cap, int Kp, int tok, CUtensorMap *map) {
-    return encode_2d(map, codes, Kp, rows_cap, Kp, GEMM_KB, tok / 2, CU_TENSOR_MAP_SWIZZLE_64B);
+    return encode_2d(map, codes, Kp, rows_cap, Kp, GEMM_KB, tok / 2, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 }  // namespace ql
 
@@ -276,7 +277,12 @@ int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_
         b->gemv_calls++;
         return QLINEAR_OK;
     }
-    const GemmPlan plan = plan_gemm(v, rows, b->num_sms);
+    int &pairs = b->gemm_pairs[v.bits == 8 ? 1 : 0];
+    if (!pairs) {
+        pairs = gemm_pair_capacity(v.bits);
+        if (!pairs) return QLINEAR_ERR_CUDA;
+    }
+    const GemmPlan plan = plan_gemm(v, rows, pairs);
     const CUtensorMap *amap = nullptr;
     st = get_amap(b, v.Kp, plan.tok, &amap);
     if (st) return st;
@@ -614,12 +620,12 @@ int qlinear_backend_stats(const qlinear_backend *b, char *buf, size_t len) {
         "\"tune_cache_misses\": 0, \"tune_calls\": 0, \"strategy_fallbacks\": 0, "
         "\"strategy_fallback_calls\": 0, \"weight_reload_calls\": 0, \"round_mode\": \"%s\", "
         "\"prepared_rows\": %d, \"kernel_launches\": %llu, \"gemv_calls\": %llu, "
-        "\"gemm_calls\": %llu}",
+        "\"gemm_calls\": %llu, \"gemm_pairs_resident\": [%d, %d]}",
         b->device, b->num_sms, b->loaded_w4, b->loaded_w8, (unsigned long long)b->weight_bytes,
         (unsigned long long)ws, b->ws_bytes ? 1 : 0,
         (unsigned long long)(b->h_in_bytes + b->h_out_bytes),
         b->round_mode == QLINEAR_ROUND_AWAY ? "away" : "even", b->prepared_rows, b->launches,
-        b->gemv_calls, b->gemm_calls);
+        b->gemv_calls, b->gemm_calls, b->gemm_pairs[0], b->gemm_pairs[1]);
     if (n < 0) return QLINEAR_ERR_PARAM;
     if (buf && len) {
         std::strncpy(buf, tmp, len - 1);
