@@ -68,11 +68,19 @@ extern "C" {
 typedef struct qlinear_backend qlinear_backend;
 typedef struct qlinear_weights qlinear_weights;
 
+/* ---- backend flags ------------------------------------------------------------------- */
+/* W4 weights normally keep two device copies: the packed nibbles (read by the HBM-bound
+ * decode GEMV) and an int8 expansion (read by the tensor-core prefill GEMM, which is
+ * compute-bound, so the doubled bytes cost little time).  With this flag only the packed
+ * copy is kept and the prefill GEMM unpacks the nibbles in shared memory instead
+ * (0.5 byte per weight instead of 1.5, at a lower prefill throughput). */
+#define QLINEAR_BACKEND_W4_PACKED_ONLY 1u
+
 typedef struct qlinear_backend_config {
     int device;     /* CUDA device ordinal (replaces the IOMMU domain id, src/npu.rs:310) */
     int round_mode; /* QLINEAR_ROUND_AWAY (default) or QLINEAR_ROUND_EVEN */
     int max_rows;   /* rows one host call may stage without reallocating; 0 = 256 */
-    int reserved;
+    unsigned flags; /* QLINEAR_BACKEND_* */
 } qlinear_backend_config;
 
 typedef struct qlinear_weight_config {
@@ -86,7 +94,7 @@ typedef struct qlinear_weight_info {
     int bits, K, N;
     int K_padded;          /* K rounded up to the GEMM's 128-element k-block */
     int N_padded;          /* N rounded up to the 128-channel tile */
-    uint64_t device_bytes; /* bytes of device memory the packed weights and scales hold */
+    uint64_t device_bytes; /* bytes of device memory the weights (all copies) and scales hold */
 } qlinear_weight_info;
 
 /* Fills cfg with defaults (device 0, ties-away, 256 rows). */

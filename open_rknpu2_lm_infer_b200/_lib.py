@@ -32,9 +32,12 @@ class QLinearUnavailable(RuntimeError):
     pass
 
 
+BACKEND_W4_PACKED_ONLY = 1
+
+
 class BackendConfig(ctypes.Structure):
     _fields_ = [("device", ctypes.c_int), ("round_mode", ctypes.c_int),
-                ("max_rows", ctypes.c_int), ("reserved", ctypes.c_int)]
+                ("max_rows", ctypes.c_int), ("flags", ctypes.c_uint)]
 
 
 class WeightConfig(ctypes.Structure):

@@ -21,10 +21,9 @@
 // of up to 8 stages:
 //   warp 0        TMA producer (both CTAs).  Activation half-tile [tok/2][128] and, for W8,
 //                 the weight tile [128][128], both counted on the leader CTA's `full`
-//                 barrier (cta_group::2 copies); for W4 the packed tile [128][64 bytes]
-//                 into this CTA's staging ring.  Weight loads of the first stages are issued
-//                 before griddepcontrol.wait, overlapping the activation-quantisation kernel
-//                 under programmatic dependent launch.
+//                 barrier (cta_group::2 copies).  W8 weight loads of the first stages are
+//                 issued before griddepcontrol.wait, overlapping the activation-quantisation
+//                 kernel under programmatic dependent launch.
 //   warp 1        tensor-memory allocation (both CTAs, pair-wide); in the leader CTA one
 //                 thread issues 4 MMAs (K=32 each) per k-block and commits them to the
 //                 barriers of both CTAs (multicast commit), freeing the smem slots and, per
@@ -33,8 +32,11 @@
 //                 part of the tensor-memory accumulator with tcgen05.ld, dequantises and
 //                 stores.  Accumulators are double-buffered (2 x tok <= 512 columns) so the
 //                 epilogue of one tile overlaps the main loop of the next.
-//   warps 10..13  (W4 only, both CTAs) converter: packed nibbles -> 8-bit codes in the
-//                 SW128 K-major layout of a separate 3-slot ring, announced to the leader.
+//   warps 10..13  (W4 only, both CTAs) converter: streams the packed weights of its 128
+//                 channels from global memory into a 4-deep register prefetch ring (no
+//                 shared-memory staging: every shared-memory byte saved shortens the stage
+//                 round trip), unpacks them into the stage's SW128 K-major A buffer once the
+//                 MMA has released the stage, and announces it to the leader.
 //                 The nibbles stay offset-binary (u = code + 8; A is declared unsigned) so
 //                 the unpack is two masks per word; the epilogue subtracts 8 * sum_k q[m][k].
 // Every mbarrier wait is bounded (common.cuh); on a timeout the pair unwinds, drains its
@@ -54,14 +56,15 @@ static_assert(KB == 128, "one 128-byte swizzle atom per row per stage");
 constexpr int CH_CTA = CH_TILE;             // 128 channels per CTA
 constexpr int CHT = 2 * CH_CTA;             // 256 channels per pair tile
 constexpr int A_SLOT = CH_CTA * KB;         // 16 KB unpacked weights per CTA
-constexpr int P_SLOT = CH_CTA * KB / 2;     // 8 KB packed W4 per CTA
-constexpr int A_SLOTS = 3;                  // converter ring depth
+constexpr int W4_PREFETCH = 4;              // converter register ring depth (k-blocks)
 constexpr int EPI_WARPS = 8;
 constexpr int MAX_DYN_SMEM = 232448;        // 227 KB opt-in per block on sm_100
 constexpr int SMEM_RESERVE = 1024 + 1024;   // alignment slack + barriers
 constexpr int MAX_STAGES = 8;
 
 struct GemmArgs {
+    const uint8_t *wq;     // W4 packed weights [Np][Kp/2] (read by the converter)
+    int Np;
     const float *wscale;
     const float *ascale;
     const int32_t *rowsum;
@@ -109,17 +112,15 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
     const int S = p.stages;
     const int tok = p.tok;
     const int b_half = (tok / 2) * KB;                    // this CTA's activation rows
-    constexpr int w_slot = BITS == 8 ? A_SLOT : P_SLOT;  // what TMA brings per k-block
-    uint8_t *sB = smem;                                   // [S][tok/2][128]
-    uint8_t *sW = sB + S * b_half;                        // [S][128][128] or [S][128][64]
-    uint8_t *sA = sW + S * w_slot;                        // W4: [3][128][128] unpacked
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sA + (BITS == 4 ? A_SLOTS * A_SLOT : 0));
+    constexpr int w_slot = A_SLOT;   // 8-bit weights per stage (TMA for W8, converter for W4)
+    uint8_t *sB = smem;              // [S][tok/2][128]
+    uint8_t *sW = sB + S * b_half;   // [S][128][128]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sW + S * w_slot);
     uint64_t *full = bars;              // [S] leader: both CTAs' TMA bytes landed
-    uint64_t *empty = full + S;         // [S] slot consumed (MMA; W4 also the converter)
-    uint64_t *pfull = empty + S;        // [S] W4: this CTA's packed tile landed
-    uint64_t *afull = pfull + S;        // [3] leader: both converters wrote the A slot
-    uint64_t *aempty = afull + A_SLOTS; // [3] MMA done with the A slot
-    uint64_t *accf = aempty + A_SLOTS;  // [2] accumulators ready for the epilogue
+    uint64_t *empty = full + S;         // [S] the MMA is done with the stage
+    uint64_t *afull = empty + S;        // [S] leader: both converters unpacked the stage
+    uint64_t *cdone = afull + S;        // [S] W4: this CTA's 128 converter threads wrote it
+    uint64_t *accf = cdone + S;         // [2] accumulators ready for the epilogue
     uint64_t *acce = accf + 2;          // [2] leader: both epilogues drained them
     uint64_t *drain = acce + 2;         // [1] leader: MMA drain on abort
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
@@ -133,12 +134,9 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], BITS == 4 ? 2 : 1);
-            mbar_init(&pfull[s], 1);
-        }
-        for (int a = 0; a < A_SLOTS; a++) {
-            mbar_init(&afull[a], 2);
-            mbar_init(&aempty[a], 1);
+            mbar_init(&empty[s], 1);
+            mbar_init(&afull[s], 2);
+            mbar_init(&cdone[s], 128);
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&accf[b], 1);
@@ -172,14 +170,9 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
             auto load_weights = [&](int s, int kb, int tc) {
-                if (BITS == 8) {
+                if (BITS == 8)
                     tma_load_2d_pair(sW + s * w_slot, &wmap, full0 + 8u * s, kb * KB,
                                      tc * CHT + (int)rank * CH_CTA);
-                } else {
-                    mbar_arrive_expect_tx(&pfull[s], P_SLOT);
-                    tma_load_2d(sW + s * w_slot, &wmap, &pfull[s], kb * (KB / 2),
-                                tc * CHT + (int)rank * CH_CTA);
-                }
                 if (rank == 0) mbar_arrive_expect_tx(&full[s], tx_pair);
             };
             // Weight tiles of the first stages do not depend on the preceding kernel:
@@ -208,7 +201,6 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                 const uint32_t first = issued > (uint32_t)S ? issued - S : 0;
                 for (uint32_t j = first; j < issued; j++) {
                     if (rank == 0) mbar_wait(&full[j % S], (j / S) & 1, nullptr, &never);
-                    if (BITS == 4) mbar_wait(&pfull[j % S], (j / S) & 1, nullptr, &never);
                 }
             }
         }
@@ -216,7 +208,7 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
         // ------------------------------------------------------------ MMA issuer (leader)
         if (lane == 0 && rank == 0) {
             const uint32_t idesc = idesc_i8(2 * CH_CTA, tok, BITS == 8, true);
-            uint32_t s = 0, ph = 0, a = 0, aph = 0, local = 0;
+            uint32_t s = 0, ph = 0, local = 0;
             bool ok = true;
             for (int t = (int)cid; t < p.num_tiles && ok; t += (int)ncl, local++) {
                 const int ab = local & 1;
@@ -225,19 +217,14 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                 const uint32_t d = tmem_base + (uint32_t)(ab * tok);
                 for (int kb = 0; kb < p.nkb; kb++) {
                     if (!(ok = mbar_wait(&full[s], ph, err, abort_flag))) break;
-                    if (BITS == 4 && !(ok = mbar_wait(&afull[a], aph, err, abort_flag))) break;
+                    if (BITS == 4 && !(ok = mbar_wait(&afull[s], ph, err, abort_flag))) break;
                     tc_fence_after();
-                    const uint64_t adesc =
-                        smem_desc_sw128_k(BITS == 8 ? sW + s * w_slot : sA + a * A_SLOT);
+                    const uint64_t adesc = smem_desc_sw128_k(sW + s * w_slot);
                     const uint64_t bdesc = smem_desc_sw128_k(sB + s * b_half);
 #pragma unroll
                     for (int k = 0; k < KB / 32; k++)
                         mma_i8_ss_pair(d, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
                     mma_commit_pair(&empty[s], 0x3);
-                    if (BITS == 4) {
-                        mma_commit_pair(&aempty[a], 0x3);
-                        if (++a == (uint32_t)A_SLOTS) { a = 0; aph ^= 1; }
-                    }
                     if (++s == (uint32_t)S) { s = 0; ph ^= 1; }
                 }
                 if (ok) mma_commit_pair(&accf[ab], 0x3);
@@ -302,40 +289,74 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
         // ------------------------------------------------------------ W4 converter
         if constexpr (BITS == 4) {
             const int ct = threadIdx.x - (2 + EPI_WARPS) * 32;  // 0..127
-            const int cp = ct & 3;  // 16-byte chunk of a 64-byte packed row (32 codes)
-            uint32_t s = 0, ph = 0, a = 0, aph = 0;
-            bool ok = true;
-            for (int t = (int)cid; t < p.num_tiles && ok; t += (int)ncl) {
-                for (int kb = 0; kb < p.nkb; kb++) {
-                    if (!(ok = mbar_wait(&pfull[s], ph, err, abort_flag))) break;
-                    if (!(ok = mbar_wait(&aempty[a], aph ^ 1, err, abort_flag))) break;
-                    const uint8_t *P = sW + s * w_slot;
-                    uint8_t *A = sA + a * A_SLOT;
+            const int cp = ct & 3;      // 16-byte quarter of a row's 64 packed bytes (32 codes)
+            const int r0 = ct >> 2;     // rows r0 + 32 j, j = 0..3
+            const long long row_bytes = (long long)p.nkb * (KB / 2);
+            // Packed codes of iteration (tile t, k-block kb) for this thread's 4 rows.
+            auto fetch = [&](uint4 (&b)[4], int t, int kb) {
+                const int n0 = (t / p.n_tok_tiles) * CHT + (int)rank * CH_CTA;
 #pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        // four threads per row (one 16-byte quarter of the 64 packed bytes each)
-                        const int row = (ct >> 2) + 32 * j;
-                        const uint4 v = *reinterpret_cast<const uint4 *>(P + row * 64 + cp * 16);
-                        // 16 packed bytes = codes k = 32*cp .. 32*cp+31 of this k-block:
-                        // word p covers 8 codes, low nibbles k 8p..8p+3, high 8p+4..8p+7.
-                        const uint4 c0 = make_uint4(v.x & 0x0F0F0F0Fu, (v.x >> 4) & 0x0F0F0F0Fu,
-                                                    v.y & 0x0F0F0F0Fu, (v.y >> 4) & 0x0F0F0F0Fu);
-                        const uint4 c1 = make_uint4(v.z & 0x0F0F0F0Fu, (v.z >> 4) & 0x0F0F0F0Fu,
-                                                    v.w & 0x0F0F0F0Fu, (v.w >> 4) & 0x0F0F0F0Fu);
-                        const int sw = row & 7;  // 128-byte swizzle of this row
-                        *reinterpret_cast<uint4 *>(A + row * 128 + (((2 * cp) ^ sw) << 4)) = c0;
-                        *reinterpret_cast<uint4 *>(A + row * 128 + (((2 * cp + 1) ^ sw) << 4)) = c1;
+                for (int j = 0; j < 4; j++) {
+                    const int n = n0 + r0 + 32 * j;
+                    b[j] = n < p.Np ? ldg_stream(p.wq + (long long)n * row_bytes + kb * (KB / 2) +
+                                                 cp * 16)
+                                    : make_uint4(0, 0, 0, 0);
+                }
+            };
+            uint4 buf[W4_PREFETCH][4];
+            int ft = (int)cid, fkb = 0;  // prefetch stream position
+#pragma unroll
+            for (int u = 0; u < W4_PREFETCH; u++) {
+                if (ft < p.num_tiles) {
+                    fetch(buf[u], ft, fkb);
+                    if (++fkb == p.nkb) { fkb = 0; ft += (int)ncl; }
+                }
+            }
+            uint32_t s = 0, ph = 0;
+            int t = (int)cid, kb = 0;
+            bool live = t < p.num_tiles;
+            while (live) {
+#pragma unroll
+                for (int u = 0; u < W4_PREFETCH; u++) {
+                    if (live) {
+                        // the MMA released the stage (its A buffer) of iteration it - S
+                        if (!mbar_wait(&empty[s], ph ^ 1, err, abort_flag)) { live = false; break; }
+                        uint8_t *A = sW + s * w_slot;
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            const int row = r0 + 32 * j;
+                            const uint4 v = buf[u][j];
+                            // word p of the 16 packed bytes covers 8 codes: low nibbles
+                            // k 8p..8p+3, high nibbles 8p+4..8p+7 (k relative to 32*cp).
+                            const uint4 c0 = make_uint4(v.x & 0x0F0F0F0Fu, (v.x >> 4) & 0x0F0F0F0Fu,
+                                                        v.y & 0x0F0F0F0Fu, (v.y >> 4) & 0x0F0F0F0Fu);
+                            const uint4 c1 = make_uint4(v.z & 0x0F0F0F0Fu, (v.z >> 4) & 0x0F0F0F0Fu,
+                                                        v.w & 0x0F0F0F0Fu, (v.w >> 4) & 0x0F0F0F0Fu);
+                            const int sw = row & 7;  // 128-byte swizzle of this row
+                            *reinterpret_cast<uint4 *>(A + row * 128 + (((2 * cp) ^ sw) << 4)) = c0;
+                            *reinterpret_cast<uint4 *>(A + row * 128 + (((2 * cp + 1) ^ sw) << 4)) = c1;
+                        }
+                        // refill this register slot with the iteration W4_PREFETCH ahead
+                        if (ft < p.num_tiles) {
+                            fetch(buf[u], ft, fkb);
+                            if (++fkb == p.nkb) { fkb = 0; ft += (int)ncl; }
+                        }
+                        // every writer makes its stores visible to the async proxy and
+                        // arrives locally; one thread collects the 128 arrivals (bounded) and
+                        // announces the stage to the leader with one cluster-scope arrive
+                        fence_proxy_async_smem();
+                        mbar_arrive(&cdone[s]);
+                        if (ct == 0) {
+                            if (!mbar_wait(&cdone[s], ph, err, abort_flag)) live = false;
+                            else mbar_arrive_remote(afull0 + 8u * s);
+                        }
+                        if (++s == (uint32_t)S) { s = 0; ph ^= 1; }
+                        if (++kb == p.nkb) {
+                            kb = 0;
+                            t += (int)ncl;
+                            live = t < p.num_tiles;
+                        }
                     }
-                    // every writer makes its stores visible to the async proxy, the four
-                    // converter warps meet, then one thread announces the slot to the leader
-                    fence_proxy_async_smem();
-                    asm volatile("bar.sync 1, 128;" ::: "memory");
-                    if (ct == 0) {
-                        mbar_arrive_remote(afull0 + 8u * a);
-                        mbar_arrive(&empty[s]);
-                    }
-                    if (++a == (uint32_t)A_SLOTS) { a = 0; aph ^= 1; }
-                    if (++s == (uint32_t)S) { s = 0; ph ^= 1; }
                 }
             }
         }
@@ -418,8 +439,8 @@ GemmPlan plan_gemm(const WeightView &w, int rows, int max_pairs) {
     int tok = (rows + tiles_m - 1) / tiles_m;
     tok = std::max(32, (tok + 31) / 32 * 32);  // 2-CTA MMA: N multiple of 32
     plan.tok = tok;
-    const int stage_bytes = (tok / 2) * KB + (w.bits == 8 ? A_SLOT : P_SLOT);
-    const int fixed = SMEM_RESERVE + (w.bits == 4 ? A_SLOTS * A_SLOT : 0);
+    const int stage_bytes = (tok / 2) * KB + A_SLOT;
+    const int fixed = SMEM_RESERVE;
     const int stages = std::min(MAX_STAGES, (MAX_DYN_SMEM - fixed) / stage_bytes);
     plan.stages = stages;
     // One CTA per SM: each CTA of the pair allocates up to 512 TMEM columns.
@@ -435,6 +456,8 @@ cudaError_t launch_gemm(const WeightView &w, const CUtensorMap &wmap, const ActV
                         int out_type, long long ldc, unsigned *err, bool pdl,
                         cudaStream_t stream) {
     GemmArgs args{};
+    args.wq = w.w;
+    args.Np = w.Np;
     args.wscale = w.scales;
     args.ascale = a.scales;
     args.rowsum = a.rowsums;

@@ -39,6 +39,9 @@ cudaError_t launch_pack_from_kn(const int8_t *codes_kn, int K, int n_total, int 
 cudaError_t launch_pack_from_checkpoint(const void *storage, const WeightView &w, uint8_t *dst,
                                         cudaStream_t stream);
 
+// int8 expansion [Np][Kp] of a packed W4 device layout (the prefill GEMM's operand).
+cudaError_t launch_expand_w4(const WeightView &w4, uint8_t *dst, cudaStream_t stream);
+
 // Decode GEMV (rows <= 8).  out [rows][ldc] of out_type; swiglu: width N/2.
 cudaError_t launch_gemv(const WeightView &w, const ActView &a, int rows, void *out, int out_type,
                         long long ldc, bool swiglu, int num_sms, cudaStream_t stream);

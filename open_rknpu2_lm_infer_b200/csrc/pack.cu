@@ -101,7 +101,29 @@ __global__ void pack_ckpt_w8_kernel(const int8_t *__restrict__ src, int K, int N
     }
 }
 
+// int8 expansion of the device W4 layout: out [Np][Kp] int8 from packed [Np][Kp/2]
+// (word w byte j = u(8w+j) | u(8w+j+4) << 4, code = u - 8).  One thread per packed word.
+__global__ void expand_w4_kernel(const uint32_t *__restrict__ packed, long long words,
+                                 uint32_t *__restrict__ out) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < words;
+         i += (long long)gridDim.x * blockDim.x) {
+        const uint32_t w = packed[i];
+        // bytes of lo: codes 8w..8w+3 (u), hi: 8w+4..8w+7; u - 8 per byte without borrows
+        const uint32_t lo = ((w & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+        const uint32_t hi = (((w >> 4) & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+        out[2 * i] = lo;
+        out[2 * i + 1] = hi;
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_expand_w4(const WeightView &w4, uint8_t *dst, cudaStream_t stream) {
+    const long long words = (long long)w4.Np * (w4.Kp / 8);
+    expand_w4_kernel<<<1024, 256, 0, stream>>>(reinterpret_cast<const uint32_t *>(w4.w), words,
+                                              reinterpret_cast<uint32_t *>(dst));
+    return cudaGetLastError();
+}
 
 cudaError_t launch_pack_from_kn(const int8_t *codes_kn, int K, int n_total, int n_begin,
                                 const WeightView &w, uint8_t *dst, cudaStream_t stream) {

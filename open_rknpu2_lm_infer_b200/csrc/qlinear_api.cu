@@ -31,6 +31,7 @@ using namespace ql;
 struct qlinear_backend {
     int device = 0;
     int round_mode = QLINEAR_ROUND_AWAY;
+    unsigned flags = 0;
     int num_sms = 148;
     int gemm_pairs[2] = {0, 0};  // resident CTA pairs of the W4 / W8 GEMM
     cudaStream_t stream = nullptr;  // host-path calls and uploads
@@ -66,11 +67,16 @@ struct qlinear_backend {
 
 struct qlinear_weights {
     qlinear_backend *backend = nullptr;
-    WeightView view{};
+    WeightView view{};         // as loaded (W4 packed or W8)
     uint8_t *d_w = nullptr;
     float *d_s = nullptr;
     uint64_t bytes = 0;
     CUtensorMap wmap{};
+    // W4 only: int8 expansion read by the prefill GEMM (absent with
+    // QLINEAR_BACKEND_W4_PACKED_ONLY)
+    WeightView view8{};
+    uint8_t *d_w8 = nullptr;
+    CUtensorMap wmap8{};
 };
 
 namespace {
@@ -277,24 +283,29 @@ int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_
         b->gemv_calls++;
         return QLINEAR_OK;
     }
-    int &pairs = b->gemm_pairs[v.bits == 8 ? 1 : 0];
+    const int gbits = (v.bits == 8 || w->d_w8) ? 8 : 4;
+    int &pairs = b->gemm_pairs[gbits == 8 ? 1 : 0];
     if (!pairs) {
-        pairs = gemm_pair_capacity(v.bits);
+        pairs = gemm_pair_capacity(gbits);
         if (!pairs) return QLINEAR_ERR_CUDA;
     }
-    const GemmPlan plan = plan_gemm(v, rows, pairs);
+    // W4 prefill reads the int8 expansion when the weights carry one
+    const bool use8 = w->d_w8 != nullptr;
+    const WeightView &gv = use8 ? w->view8 : v;
+    const CUtensorMap &gmap = use8 ? w->wmap8 : w->wmap;
+    const GemmPlan plan = plan_gemm(gv, rows, pairs);
     const CUtensorMap *amap = nullptr;
     st = get_amap(b, v.Kp, plan.tok, &amap);
     if (st) return st;
     if (!swiglu) {
-        QL_TRY(launch_gemm(v, w->wmap, av, *amap, plan, rows, c_dev, c_type, ldc, b->d_err,
-                           true, stream));
+        QL_TRY(launch_gemm(gv, gmap, av, *amap, plan, rows, c_dev, c_type, ldc, b->d_err, true,
+                           stream));
         b->launches++;
     } else {
         st = ensure_dev(reinterpret_cast<void **>(&b->d_y), &b->y_elems,
                         (size_t)rows * v.N * sizeof(float));
         if (st) return st;
-        QL_TRY(launch_gemm(v, w->wmap, av, *amap, plan, rows, b->d_y, kF32, v.N, b->d_err, true,
+        QL_TRY(launch_gemm(gv, gmap, av, *amap, plan, rows, b->d_y, kF32, v.N, b->d_err, true,
                            stream));
         QL_TRY(launch_swiglu(b->d_y, rows, v.N, c_dev, c_type, ldc, stream));
         b->launches += 2;
@@ -328,6 +339,7 @@ qlinear_weights *weights_create_common(qlinear_backend *b, const qlinear_weight_
     void *tmp = nullptr;
     auto cleanup = [&](int status) -> qlinear_weights * {
         cudaFree(tmp);
+        cudaFree(w->d_w8);
         cudaFree(w->d_w);
         cudaFree(w->d_s);
         delete w;
@@ -360,6 +372,19 @@ qlinear_weights *weights_create_common(qlinear_backend *b, const qlinear_weight_
     tmp = nullptr;
     if (!encode_weight_map(v, &w->wmap)) return cleanup(QLINEAR_ERR_CUDA);
     w->bytes = wbytes + (uint64_t)v.Np * sizeof(float);
+    if (v.bits == 4 && !(b->flags & QLINEAR_BACKEND_W4_PACKED_ONLY)) {
+        const size_t bytes8 = (size_t)v.Np * v.Kp;
+        if ((e = cudaMalloc(&w->d_w8, bytes8)) != cudaSuccess) return cleanup(cuda_status(e));
+        w->view8 = v;
+        w->view8.bits = 8;
+        w->view8.w = w->d_w8;
+        if ((e = launch_expand_w4(v, w->d_w8, b->stream)) != cudaSuccess ||
+            (e = cudaStreamSynchronize(b->stream)) != cudaSuccess)
+            return cleanup(cuda_status(e));
+        b->launches++;
+        if (!encode_weight_map(w->view8, &w->wmap8)) return cleanup(QLINEAR_ERR_CUDA);
+        w->bytes += bytes8;
+    }
     b->weight_bytes += w->bytes;
     (v.bits == 4 ? b->loaded_w4 : b->loaded_w8)++;
     b->max_kp = std::max(b->max_kp, v.Kp);
@@ -386,7 +411,8 @@ qlinear_backend *qlinear_backend_create(const qlinear_backend_config *cfg) {
     if (!cfg) cfg = &def;
     if (cfg->round_mode != QLINEAR_ROUND_AWAY && cfg->round_mode != QLINEAR_ROUND_EVEN)
         return fail(QLINEAR_ERR_PARAM), nullptr;
-    if (cfg->max_rows < 0) return fail(QLINEAR_ERR_PARAM), nullptr;
+    if (cfg->max_rows < 0 || (cfg->flags & ~QLINEAR_BACKEND_W4_PACKED_ONLY))
+        return fail(QLINEAR_ERR_PARAM), nullptr;
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || cfg->device < 0 || cfg->device >= ndev)
         return fail(ndev == 0 ? QLINEAR_ERR_CUDA : QLINEAR_ERR_PARAM), nullptr;
@@ -400,6 +426,7 @@ qlinear_backend *qlinear_backend_create(const qlinear_backend_config *cfg) {
     if (!b) return fail(QLINEAR_ERR_ALLOC), nullptr;
     b->device = cfg->device;
     b->round_mode = cfg->round_mode;
+    b->flags = cfg->flags;
     b->num_sms = prop.multiProcessorCount;
     b->prepared_rows = cfg->max_rows ? cfg->max_rows : 256;
     if (cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking) != cudaSuccess ||
@@ -473,6 +500,7 @@ void qlinear_weights_free(qlinear_weights *w) {
     DeviceGuard guard(b->device);
     cudaStreamSynchronize(b->stream);
     cudaFree(w->d_w);
+    cudaFree(w->d_w8);
     cudaFree(w->d_s);
     b->weight_bytes -= w->bytes;
     (w->view.bits == 4 ? b->loaded_w4 : b->loaded_w8)--;

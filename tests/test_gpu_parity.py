@@ -235,3 +235,35 @@ def test_errors_are_status_codes(backend):
     out = torch.zeros((4, 256), dtype=torch.float16, device="cuda")
     with pytest.raises(NpuError):
         lin.run_device(dev(x), out, 4, ldc=100)
+
+
+@pytest.mark.parametrize("rows", [9, 40, 300, 512])
+def test_w4_packed_only_backend(coracle, rows):
+    """The memory-lean mode (QLINEAR_BACKEND_W4_PACKED_ONLY): the prefill GEMM unpacks the
+    nibbles in shared memory; results must be identical to the oracle (and therefore to
+    the default mode, which reads an int8 expansion)."""
+    from open_rknpu2_lm_infer_b200 import Backend
+    b = Backend(device=0, w4_packed_only=True)
+    k, n = 2560, 1024
+    w = W.weight_codes(4, k, n, stream=70)
+    sw = W.weight_scales(n, stream=70)
+    xh = W.activations(rows, k, stream=71)
+    lin = b.load(QuantMatrix(4, k, n, w, sw))
+    assert lin.device_bytes < k * n  # packed only: 0.5 byte per weight (+ scales)
+    y, acc = coracle.linear(w, sw, xh, want_acc=True)
+    out = torch.zeros((rows, n), dtype=torch.float16, device="cuda")
+    acc_gpu = torch.zeros((rows, n), dtype=torch.int32, device="cuda")
+    a = dev(xh)
+    lin.run_device(a, out, rows)
+    lin.run_device(a, acc_gpu, rows)
+    b.check()
+    np.testing.assert_array_equal(acc_gpu.cpu().numpy(), acc)
+    np.testing.assert_array_equal(out.cpu().numpy(), y.astype(np.float16))
+    lin.close()
+    b.close()
+
+
+def test_w4_default_keeps_int8_copy(backend):
+    k, n = 512, 256
+    lin = backend.load(QuantMatrix(4, k, n, W.weight_codes(4, k, n), W.weight_scales(n)))
+    assert lin.device_bytes >= k * n + k * n // 2
