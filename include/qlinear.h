@@ -52,6 +52,7 @@ extern "C" {
 #define QLINEAR_ERR_TIMEOUT (-5)     /* a bounded device-side wait gave up */
 #define QLINEAR_ERR_NCCL (-6)        /* an NCCL call failed */
 #define QLINEAR_ERR_STATE (-7)       /* object used in the wrong state */
+#define QLINEAR_ERR_LIMIT (-8)       /* request exceeds a fixed maximum (see the call's limits) */
 
 /* ---- rounding of the activation quantiser ------------------------------------------ */
 #define QLINEAR_ROUND_AWAY 0 /* f32::round, ties away from zero: the reference (src/npu.rs:1109) */
@@ -177,6 +178,31 @@ QLINEAR_API int qlinear_interleave_columns(qlinear_backend *backend, const void 
 QLINEAR_API int qlinear_backend_profile(qlinear_backend *backend, int enable);
 QLINEAR_API int qlinear_backend_profile_collect(qlinear_backend *backend, double *quant_ms,
                                                 double *main_ms, int *calls);
+
+/* Allocation-free decode call.  No counterpart in the reference.  For callers that cannot
+ * allocate device memory while they run a layer: a process whose device memory is
+ * entirely reserved up front by its own pool allocator, or a latency-critical decode loop
+ * that must not call cudaMalloc/cudaFree (which can synchronise the device and stall every
+ * stream).  Same arithmetic and results as qlinear_run_device (plain output, no SwiGLU),
+ * but the activation codes, scales and row sums live in a fixed scratch array compiled
+ * into the library (a file-scope __device__ array of QLINEAR_NOALLOC_SCRATCH_BYTES, held by
+ * every GPU that loads the library until the process exits) instead of the backend's
+ * workspace.  The call allocates nothing, on the device or the host.
+ *   Limits: rows <= QLINEAR_NOALLOC_MAX_ROWS and K (rounded up to 128) <= QLINEAR_NOALLOC_MAX_K;
+ *   larger requests return QLINEAR_ERR_LIMIT without launching anything.
+ *   The first call on a device looks the scratch up (cudaGetSymbolAddress, which may load
+ *   the library's device code on that device); make that first call before any stream
+ *   capture.
+ *   All calls on a device share the one scratch array: calls whose kernels can overlap on
+ *   the GPU (different streams, or different host threads) race and corrupt each other's
+ *   codes.  Order them on one stream.  Each call rewrites everything it reads back. */
+#define QLINEAR_NOALLOC_MAX_ROWS 8
+#define QLINEAR_NOALLOC_MAX_K 16384
+#define QLINEAR_NOALLOC_SCRATCH_BYTES \
+    (QLINEAR_NOALLOC_MAX_ROWS * QLINEAR_NOALLOC_MAX_K + 8 * QLINEAR_NOALLOC_MAX_ROWS)
+QLINEAR_API int qlinear_run_device_noalloc(const qlinear_weights *weights, const void *a_dev,
+                                           int a_type, void *c_dev, int c_type, long long ldc,
+                                           int rows, void *stream);
 
 /* Reads and clears the backend's device error word (bounded waits that gave up);
  * synchronizes `stream` first.  Returns QLINEAR_OK or QLINEAR_ERR_TIMEOUT. */

@@ -20,6 +20,9 @@ QLINEAR_ERR_UNSUPPORTED = -4
 QLINEAR_ERR_TIMEOUT = -5
 QLINEAR_ERR_NCCL = -6
 QLINEAR_ERR_STATE = -7
+QLINEAR_ERR_LIMIT = -8
+NOALLOC_MAX_ROWS = 8
+NOALLOC_MAX_K = 16384
 
 ROUND_AWAY = 0
 ROUND_EVEN = 1
@@ -68,6 +71,7 @@ SIGNATURES = {
     "qlinear_run_swiglu_f32": (_I, [_P, _P, _P, _P, _I]),
     "qlinear_run_device": (_I, [_P, _P, _P, _I, _P, _I, ctypes.c_longlong, _I, ctypes.c_uint, _P]),
     "qlinear_act_quant_device": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _P]),
+    "qlinear_run_device_noalloc": (_I, [_P, _P, _I, _P, _I, ctypes.c_longlong, _I, _P]),
     "qlinear_interleave_columns": (_I, [_P, _P, _P, _I, _I, _I, _I, _P]),
     "qlinear_backend_profile": (_I, [_P, _I]),
     "qlinear_backend_profile_collect": (_I, [_P, ctypes.POINTER(ctypes.c_double),

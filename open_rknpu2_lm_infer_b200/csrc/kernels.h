@@ -73,6 +73,14 @@ cudaError_t launch_swiglu(const float *y, int rows, int N, void *out, int out_ty
 cudaError_t launch_interleave(const void *src, void *dst, int shards, int rows, int shard_cols,
                               int elem_bytes, int num_sms, cudaStream_t stream);
 
+// Weights view, device and backend settings of a weights object (qlinear_api.cu), for the
+// allocation-free decode call (noalloc.cu).
+}  // namespace ql
+struct qlinear_weights;
+namespace ql {
+bool weights_for_noalloc(const qlinear_weights *w, WeightView *view, int *device, int *round_mode,
+                         int *num_sms);
+
 // TMA descriptor encoding through the driver entry point (no -lcuda link needed).
 bool tma_available();
 bool encode_weight_map(const WeightView &w, CUtensorMap *map);

@@ -394,6 +394,19 @@ qlinear_weights *weights_create_common(qlinear_backend *b, const qlinear_weight_
 
 }  // namespace
 
+// What the allocation-free decode call (noalloc.cu) needs from a weights object.
+namespace ql {
+bool weights_for_noalloc(const qlinear_weights *w, WeightView *view, int *device, int *round_mode,
+                         int *num_sms) {
+    if (!w || !w->backend) return false;
+    *view = w->view;
+    *device = w->backend->device;
+    *round_mode = w->backend->round_mode;
+    *num_sms = w->backend->num_sms;
+    return true;
+}
+}  // namespace ql
+
 // ====================================================================== C ABI
 extern "C" {
 
@@ -674,6 +687,7 @@ const char *qlinear_strerror(int status) {
     case QLINEAR_ERR_TIMEOUT: return "device wait timed out";
     case QLINEAR_ERR_NCCL: return "NCCL error";
     case QLINEAR_ERR_STATE: return "invalid state";
+    case QLINEAR_ERR_LIMIT: return "request exceeds a fixed limit of this call";
     default: return "unknown status";
     }
 }
