@@ -64,6 +64,7 @@ def parse():
                     help="target CPU time of the oracle baseline sample")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
     return ap.parse_args()
 
 
@@ -346,7 +347,7 @@ def run_ours(args, rank, world, local_rank):
         line["e2e"] = e2e_measure(backend, lin, torch, dist, dev, args, world, m, k, n, ns,
                                   x_host, y_gather)
 
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and not args.no_cpu:
         ops_s, rows, dt, threads = oracle_sample(bits, k, n, m, args.cpu_seconds)
         cores, model = cpu_info()
         line["cpu_baseline"] = {
