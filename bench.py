@@ -39,10 +39,10 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-# DRAM traffic of the dominant kernel per launch (dram__bytes_read.sum +
-# dram__bytes_write.sum) from the ncu capture summarised in
-# profiles/gemm_w4a8_cfg4_m512.md; None until a capture exists for this build.
-GEMM_TRAFFIC_BYTES = None
+# DRAM traffic of the dominant kernel per launch on the default workload
+# (dram__bytes_read.sum + dram__bytes_write.sum = 246.35 MB + 19.03 MB) from the ncu capture
+# summarised in profiles/gemm_w4a8_cfg4_m512.md (same workload, one GPU).
+GEMM_TRAFFIC_BYTES = 265_384_704
 
 WORKLOADS = {
     # name: (bits, K, N, M, description)
@@ -320,8 +320,9 @@ def run_ours(args, rank, world, local_rank):
                 "peak_source": "int8 dense, measured by bench.py: cuBLASLt (torch._int_mm) "
                                "8192^3 burst; MEASURED_PEAKS.json has no int8 figure",
                 "frac_of_nominal_4500": achieved / 4500.0,
-                "traffic": GEMM_TRAFFIC_BYTES,
-                "kernel": "gemm_kernel<4> (tcgen05 kind::i8)",
+                "traffic": GEMM_TRAFFIC_BYTES if (args.workload == "cfg4" and world == 1) else None,
+                "traffic_source": "ncu dram bytes, profiles/gemm_w4a8_cfg4_m512.md",
+                "kernel": "gemm_kernel (tcgen05.mma.cta_group::2 kind::i8, CTA pairs)",
                 "kernel_ms": per_launch * 1e3, "act_quant_ms": quant_s / max(calls, 1) * 1e3}
 
     line = {
