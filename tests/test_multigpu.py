@@ -1,0 +1,55 @@
+"""Split-N on 2+ GPUs (NCCL): the assembled output equals the single-GPU output bitwise.
+Runs as torchrun child processes; skipped when fewer than 2 GPUs are visible."""
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+CHILD = r"""
+import os, sys, datetime
+sys.path.insert(0, os.environ["QL_ROOT"])
+import numpy as np, torch, torch.distributed as dist
+from open_rknpu2_lm_infer_b200 import Backend, QuantMatrix
+from open_rknpu2_lm_infer_b200 import workloads as W
+from open_rknpu2_lm_infer_b200.sharded import ShardedLinear
+rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+torch.cuda.set_device(rank)
+dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
+                        device_id=torch.device("cuda", rank))
+b = Backend(device=rank)
+for bits, k, n, rows in [(4, 2560, 4096, 300), (8, 4096, 2048, 3), (4, 8192, 28672 // 4, 64)]:
+    qm = QuantMatrix(bits, k, n, W.weight_codes(bits, k, n, stream=n), W.weight_scales(n, stream=n))
+    x = torch.from_numpy(W.activations(rows, k, stream=rows)).cuda()
+    sh = ShardedLinear(b, qm)
+    out = torch.empty((rows, n), dtype=torch.float16, device="cuda")
+    sh.run_device(x, out, rows)
+    full = b.load(qm)
+    want = torch.empty((rows, n), dtype=torch.float16, device="cuda")
+    full.run_device(x, want, rows)
+    torch.cuda.synchronize()
+    assert torch.equal(out, want), (rank, bits, k, n, rows)
+    sh.linear.close(); full.close()
+b.check()
+dist.barrier()
+dist.destroy_process_group()
+print(f"rank {rank} ok")
+"""
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_sharded_equals_single_gpu(tmp_path):
+    script = tmp_path / "child.py"
+    script.write_text(CHILD)
+    env = dict(os.environ, QL_ROOT=ROOT, NCCL_NVLS_ENABLE="0")
+    n = min(torch.cuda.device_count(), 4)
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", f"--nproc-per-node={n}", "--master-addr", "127.0.0.1",
+           "--master-port", "29531", str(script)]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
