@@ -21,7 +21,6 @@
 #include "common.cuh"
 #include "kernels.h"
 
-#include <float.h>
 
 namespace ql {
 
@@ -59,13 +58,6 @@ struct Vec<float> {
 __device__ __forceinline__ float to_f32(float v) { return v; }
 __device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
 
-__device__ __forceinline__ int quant_code(float v, float inv, int round_mode) {
-    float s = __fmul_rn(v, inv);
-    float r = round_mode ? rintf(s) : roundf(s);
-    int q = (r != r) ? 0 : __float2int_rz(r);
-    return max(-127, min(127, q));
-}
-
 __device__ __forceinline__ float block_max(float v, float *red) {
 #pragma unroll
     for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -96,11 +88,6 @@ __device__ __forceinline__ int block_sum(int v, int *red) {
     }
     __syncthreads();
     return red[0];
-}
-
-__device__ __forceinline__ void row_scale(float amax, float &scale, float &inv) {
-    scale = amax == 0.0f ? 1.0f : fmaxf(__fdiv_rn(amax, 127.0f), FLT_MIN);
-    inv = __fdiv_rn(1.0f, scale);
 }
 
 // Vectorised path: K % VEC == 0 and every row 16-byte aligned.
@@ -141,7 +128,7 @@ __global__ void __launch_bounds__(kThreads) act_quant_vec_kernel(
     }
     amax = block_max(amax, redf);
     float scale, inv;
-    row_scale(amax, scale, inv);
+    a8_row_scale(amax, scale, inv);
 
     int sum = 0;
     auto emit = [&](int c, const uint4 &rv) {
@@ -153,7 +140,7 @@ __global__ void __launch_bounds__(kThreads) act_quant_vec_kernel(
             uint32_t packed = 0;
 #pragma unroll
             for (int e = 0; e < 4; e++) {
-                const int q = quant_code(t[4 * g + e], inv, round_mode);
+                const int q = a8_code(t[4 * g + e], inv, round_mode);
                 sum += q;
                 packed |= (uint32_t)(q & 0xff) << (8 * e);
             }
@@ -193,10 +180,10 @@ __global__ void __launch_bounds__(kThreads) act_quant_scalar_kernel(
     for (int k = threadIdx.x; k < K; k += kThreads) amax = fmaxf(amax, fabsf(to_f32(xr[k])));
     amax = block_max(amax, redf);
     float scale, inv;
-    row_scale(amax, scale, inv);
+    a8_row_scale(amax, scale, inv);
     int sum = 0;
     for (int k = threadIdx.x; k < K; k += kThreads) {
-        const int q = quant_code(to_f32(xr[k]), inv, round_mode);
+        const int q = a8_code(to_f32(xr[k]), inv, round_mode);
         sum += q;
         cr[k] = (int8_t)q;
     }

@@ -100,6 +100,16 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
         : "memory");
 }
+// Untiled bulk copy global -> this CTA's shared memory, completion counted on `bar`
+// (both addresses 16-byte aligned, size a multiple of 16).  No multicast.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
+                                          uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
 // Generic-proxy shared-memory writes -> visible to the async proxy (tensor core, TMA).
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -274,6 +284,22 @@ __device__ __forceinline__ uint4 ldg_stream(const void *p) {
     return v;
 }
 
+
+// ------------------------------------------------------------------ the A8 quantiser
+// (src/npu.rs:1099-1110): scale = amax == 0 ? 1 : max(amax / 127, FLT_MIN) and inv = 1 / scale
+// (IEEE divisions); q = clamp(round(x * inv), -127, 127) with round = roundf (ties away from
+// zero; rintf for QLINEAR_ROUND_EVEN), NaN -> 0 like Rust's `NaN as i32`.  Shared by the
+// stand-alone quantisation kernel and the fused decode GEMV so both give identical codes.
+__device__ __forceinline__ void a8_row_scale(float amax, float &scale, float &inv) {
+    scale = amax == 0.0f ? 1.0f : fmaxf(__fdiv_rn(amax, 127.0f), 1.17549435e-38f);
+    inv = __fdiv_rn(1.0f, scale);
+}
+__device__ __forceinline__ int a8_code(float v, float inv, int round_mode) {
+    const float s = __fmul_rn(v, inv);
+    const float r = round_mode ? rintf(s) : roundf(s);
+    const int q = (r != r) ? 0 : __float2int_rz(r);
+    return max(-127, min(127, q));
+}
 
 // Output element store helpers (f32 / f16 / raw i32).
 template <typename T>

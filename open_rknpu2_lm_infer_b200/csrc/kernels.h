@@ -7,7 +7,7 @@
 
 namespace ql {
 
-enum ElemType { kF32 = 0, kF16 = 1, kI32 = 2 };
+enum ElemType { kF32 = 0, kF16 = 1, kI32 = 2, kI8Codes = 3 };
 
 // Device weight layout (see pack.cu):
 //   W8: int8 [Np][Kp], row n holds codes w[k][n] for k < K, zero padding.
@@ -42,9 +42,24 @@ cudaError_t launch_pack_from_checkpoint(const void *storage, const WeightView &w
 // int8 expansion [Np][Kp] of a packed W4 device layout (the prefill GEMM's operand).
 cudaError_t launch_expand_w4(const WeightView &w4, uint8_t *dst, cudaStream_t stream);
 
-// Decode GEMV (rows <= 8).  out [rows][ldc] of out_type; swiglu: width N/2.
-cudaError_t launch_gemv(const WeightView &w, const ActView &a, int rows, void *out, int out_type,
-                        long long ldc, bool swiglu, int num_sms, cudaStream_t stream);
+// Decode GEMV (rows <= 8).  Input either activation codes from the quantisation kernel
+// (type kI8Codes: x = codes [rows][Kp], ascale / rowsum set) or raw activations (kF16 /
+// kF32: x = [rows][ldx], K % (16 / elem) == 0, ldx likewise, x 16-byte aligned), which the
+// GEMV quantises itself.  out [rows][ldc] of out_type; swiglu: width N/2.
+struct GemvInput {
+    const void *x;
+    int type;
+    long long ldx;
+    int round_mode;
+    const float *ascale;
+    const int32_t *rowsum;
+    unsigned *err;  // device error word (bounded waits)
+};
+// rows <= 8 and the activation codes and the CTA's weight scales fit the GEMV's shared memory
+bool gemv_fits(int rows, int Kp, int N, int bits, bool swiglu, int num_sms);
+bool gemv_can_fuse(const void *x, int type, long long ldx, int K);
+cudaError_t launch_gemv(const WeightView &w, const GemvInput &in, int rows, void *out,
+                        int out_type, long long ldc, bool swiglu, int num_sms, cudaStream_t stream);
 
 // tcgen05 GEMM (any rows).  wmap / amap are the TMA descriptors of the weights and the
 // activation codes (see encode_* below).  out [rows][ldc] of out_type.

@@ -76,8 +76,8 @@ extern "C" int qlinear_run_device_noalloc(const qlinear_weights *weights, const 
                              rowsums, s) != cudaSuccess)
             status = QLINEAR_ERR_CUDA;
         else {
-            ActView av{codes, scales, rowsums, kMaxRows};
-            if (launch_gemv(v, av, rows, c_dev, c_type, ldc, false, num_sms, s) != cudaSuccess)
+            GemvInput in{codes, kI8Codes, v.Kp, round_mode, scales, rowsums, nullptr};
+            if (launch_gemv(v, in, rows, c_dev, c_type, ldc, false, num_sms, s) != cudaSuccess)
                 status = QLINEAR_ERR_CUDA;
         }
     }

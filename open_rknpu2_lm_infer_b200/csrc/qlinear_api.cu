@@ -256,9 +256,24 @@ int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_
     if (ldc < width) return QLINEAR_ERR_PARAM;
     if ((flags & ~QLINEAR_RUN_SWIGLU) != 0) return QLINEAR_ERR_PARAM;
 
-    int st = ensure_act_ws(b, rows, v.Kp);
-    if (st) return st;
+    int st;
     const std::array<cudaEvent_t, 3> *ev = nullptr;
+    if (gemv_fits(rows, v.Kp, v.N, v.bits, swiglu, b->num_sms) && gemv_can_fuse(a_dev, a_type, v.K, v.K)) {
+        // decode: one kernel that quantises the rows itself and streams the weights
+        if (b->profiling) {
+            if ((st = next_prof_events(b, &ev))) return st;
+            QL_TRY(cudaEventRecord((*ev)[0], stream));
+            QL_TRY(cudaEventRecord((*ev)[1], stream));
+        }
+        GemvInput in{a_dev, a_type, v.K, b->round_mode, nullptr, nullptr, b->d_err};
+        const cudaError_t e = launch_gemv(v, in, rows, c_dev, c_type, ldc, swiglu, b->num_sms, stream);
+        if (ev) cudaEventRecord((*ev)[2], stream);
+        QL_TRY(e);
+        b->launches++;
+        b->gemv_calls++;
+        return QLINEAR_OK;
+    }
+    if ((st = ensure_act_ws(b, rows, v.Kp))) return st;
     if (b->profiling) {
         if ((st = next_prof_events(b, &ev))) return st;
         QL_TRY(cudaEventRecord((*ev)[0], stream));
@@ -277,8 +292,9 @@ int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_
     } stop{ev, stream};
     ActView av{codes, b->d_ascale, b->d_rowsum, (int)(b->ws_bytes / v.Kp)};
 
-    if (rows <= 8) {
-        QL_TRY(launch_gemv(v, av, rows, c_dev, c_type, ldc, swiglu, b->num_sms, stream));
+    if (gemv_fits(rows, v.Kp, v.N, v.bits, swiglu, b->num_sms)) {
+        GemvInput in{codes, kI8Codes, v.Kp, b->round_mode, b->d_ascale, b->d_rowsum, b->d_err};
+        QL_TRY(launch_gemv(v, in, rows, c_dev, c_type, ldc, swiglu, b->num_sms, stream));
         b->launches++;
         b->gemv_calls++;
         return QLINEAR_OK;
