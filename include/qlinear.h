@@ -145,6 +145,16 @@ QLINEAR_API int qlinear_run_f32(qlinear_backend *backend, const qlinear_weights 
 QLINEAR_API int qlinear_run_swiglu_f32(qlinear_backend *backend, const qlinear_weights *weights,
                            const float *a_host, float *c_host, int rows);
 
+/* The host path writing into a wider output: c_host f32 rows of stride ldc >= the output
+ * width (N, or N/2 with QLINEAR_RUN_SWIGLU in flags), columns [0, width) of each row;
+ * the rest of each row is left untouched.  This is what Projection::run_from
+ * (src/model/projection.rs:200-232) does with a scratch buffer and a row-by-row copy when a
+ * fused projection is stored as several linears (mixed bit widths): each part writes its
+ * column range of the fused [rows][width] output directly (pass c_host + column offset). */
+QLINEAR_API int qlinear_run_f32_ex(qlinear_backend *backend, const qlinear_weights *weights,
+                                   const float *a_host, float *c_host, long long ldc, int rows,
+                                   unsigned flags);
+
 /* Device-resident path (no reference counterpart; the benchmark and multi-GPU path):
  * a_dev [rows][K] of a_type (QLINEAR_F16 or QLINEAR_F32), c_dev [rows][ldc] of c_type
  * (QLINEAR_F16, QLINEAR_F32 or QLINEAR_I32 raw accumulators), ldc >= output width

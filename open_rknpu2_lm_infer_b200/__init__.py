@@ -6,7 +6,8 @@ reference's ``npu::Backend / Linear / QuantMatrix`` API (``open_rknpu2_lm_infer_
 and the C ABI of ``include/qlinear.h`` (``lib/libqlinear_b200.so``).
 """
 from .npu import Backend, Linear, NpuError, QuantMatrix  # noqa: F401
+from .projection import MatrixLoader, Projection, concatenate  # noqa: F401
 from ._lib import LIB_PATH, QLinearUnavailable, ROUND_AWAY, ROUND_EVEN  # noqa: F401
 
 __all__ = ["Backend", "Linear", "NpuError", "QuantMatrix", "LIB_PATH", "QLinearUnavailable",
-           "ROUND_AWAY", "ROUND_EVEN"]
+           "ROUND_AWAY", "ROUND_EVEN", "MatrixLoader", "Projection", "concatenate"]

@@ -69,6 +69,7 @@ SIGNATURES = {
     "qlinear_backend_prepare": (_I, [_P, _I]),
     "qlinear_run_f32": (_I, [_P, _P, _P, _P, _I]),
     "qlinear_run_swiglu_f32": (_I, [_P, _P, _P, _P, _I]),
+    "qlinear_run_f32_ex": (_I, [_P, _P, _P, _P, ctypes.c_longlong, _I, ctypes.c_uint]),
     "qlinear_run_device": (_I, [_P, _P, _P, _I, _P, _I, ctypes.c_longlong, _I, ctypes.c_uint, _P]),
     "qlinear_act_quant_device": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _P]),
     "qlinear_run_device_noalloc": (_I, [_P, _P, _I, _P, _I, ctypes.c_longlong, _I, _P]),

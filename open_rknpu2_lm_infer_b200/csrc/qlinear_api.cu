@@ -559,13 +559,15 @@ int qlinear_run_device(qlinear_backend *b, const qlinear_weights *w, const void 
 }
 
 static int run_host(qlinear_backend *b, const qlinear_weights *w, const float *a_host,
-                    float *c_host, int rows, unsigned flags) {
+                    float *c_host, long long ldc, int rows, unsigned flags) {
     if (!b || !w || w->backend != b || !a_host || !c_host || rows < 1) return QLINEAR_ERR_PARAM;
+    if ((flags & ~QLINEAR_RUN_SWIGLU) != 0) return QLINEAR_ERR_PARAM;
     DeviceGuard guard(b->device);
     const WeightView &v = w->view;
     const bool swiglu = (flags & QLINEAR_RUN_SWIGLU) != 0;
     if (swiglu && v.N % 2) return QLINEAR_ERR_PARAM;
     const int width = swiglu ? v.N / 2 : v.N;
+    if (ldc < width) return QLINEAR_ERR_PARAM;
     const size_t in_bytes = (size_t)rows * v.K * sizeof(float);
     const size_t out_bytes = (size_t)rows * width * sizeof(float);
     int st;
@@ -587,18 +589,31 @@ static int run_host(qlinear_backend *b, const qlinear_weights *w, const float *a
         cudaStreamSynchronize(b->stream);
         return QLINEAR_ERR_TIMEOUT;
     }
-    std::memcpy(c_host, b->h_out, out_bytes);
+    if (ldc == width) {
+        std::memcpy(c_host, b->h_out, out_bytes);
+    } else {
+        const float *src = static_cast<const float *>(b->h_out);
+        for (int r = 0; r < rows; r++)
+            std::memcpy(c_host + (size_t)r * ldc, src + (size_t)r * width, (size_t)width * sizeof(float));
+    }
     return QLINEAR_OK;
 }
 
 int qlinear_run_f32(qlinear_backend *b, const qlinear_weights *w, const float *a_host,
                     float *c_host, int rows) {
-    return run_host(b, w, a_host, c_host, rows, 0);
+    const long long width = w ? w->view.N : 0;
+    return run_host(b, w, a_host, c_host, width, rows, 0);
 }
 
 int qlinear_run_swiglu_f32(qlinear_backend *b, const qlinear_weights *w, const float *a_host,
                            float *c_host, int rows) {
-    return run_host(b, w, a_host, c_host, rows, QLINEAR_RUN_SWIGLU);
+    const long long width = w ? w->view.N / 2 : 0;
+    return run_host(b, w, a_host, c_host, width, rows, QLINEAR_RUN_SWIGLU);
+}
+
+int qlinear_run_f32_ex(qlinear_backend *b, const qlinear_weights *w, const float *a_host,
+                       float *c_host, long long ldc, int rows, unsigned flags) {
+    return run_host(b, w, a_host, c_host, ldc, rows, flags);
 }
 
 int qlinear_act_quant_device(qlinear_backend *b, const void *a_dev, int a_type, int rows, int K,

@@ -273,6 +273,26 @@ class Linear:
         self._host(input, output, rows, True)
         return True
 
+    def run_columns(self, input: np.ndarray, output: np.ndarray, rows: int, ldc: int,
+                    col: int = 0, swiglu: bool = False) -> None:
+        """f32 [rows][K] -> columns [col, col + width) of the f32 rows of stride `ldc` in
+        `output` (width = N, or N/2 with swiglu); the rest of each row is untouched.  One
+        part of a fused projection (src/model/projection.rs:215-228) written in place."""
+        if rows < 1:
+            raise ValueError("linear batch must be >= 1")
+        width = self._n // 2 if swiglu else self._n
+        input = np.asarray(input)
+        if input.dtype != np.float32 or output.dtype != np.float32:
+            raise TypeError("Linear.run_columns takes f32 buffers")
+        if not (input.flags.c_contiguous and output.flags.c_contiguous):
+            raise ValueError("buffers must be C-contiguous")
+        if (col < 0 or ldc < col + width or input.size < rows * self._k
+                or output.size < (rows - 1) * ldc + col + width):
+            raise ValueError("linear input/output shape mismatch")
+        _check(self._lib.qlinear_run_f32_ex(
+            self._backend.raw, self._raw, input.ctypes.data, output.ctypes.data + 4 * col, ldc,
+            rows, L.RUN_SWIGLU if swiglu else 0), f"W{self.bits} run")
+
     def run_device(self, a, out, rows: int, swiglu: bool = False, ldc: int | None = None,
                    stream=None, out_type: int | None = None) -> None:
         """Device-resident call: `a` [rows][K] fp16/f32 and `out` [rows][ldc] (fp16, f32 or
