@@ -76,6 +76,12 @@ typedef struct qlinear_weights qlinear_weights;
  * copy is kept and the prefill GEMM unpacks the nibbles in shared memory instead
  * (0.5 byte per weight instead of 1.5, at a lower prefill throughput). */
 #define QLINEAR_BACKEND_W4_PACKED_ONLY 1u
+/* Let the prefill GEMM use its stream-K schedule where whole tiles would leave CTA pairs
+ * idle (every pair then takes the same number of k-blocks; split tiles are summed exactly
+ * in an int32 workspace, so results are bit-identical).  Off by default: on B200 the pass
+ * that finishes split tiles is bound by the epilogue's output stores and loses to the
+ * whole-tile schedule on every shape measured so far. */
+#define QLINEAR_BACKEND_GEMM_STREAM_K 2u
 
 typedef struct qlinear_backend_config {
     int device;     /* CUDA device ordinal (replaces the IOMMU domain id, src/npu.rs:310) */

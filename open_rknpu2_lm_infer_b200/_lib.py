@@ -36,6 +36,7 @@ class QLinearUnavailable(RuntimeError):
 
 
 BACKEND_W4_PACKED_ONLY = 1
+BACKEND_GEMM_STREAM_K = 2
 
 
 class BackendConfig(ctypes.Structure):

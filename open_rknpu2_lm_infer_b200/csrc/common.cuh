@@ -276,6 +276,26 @@ __device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
 }
 
 // 16-byte streaming load that does not allocate in L1 (weights are read once).
+// L2 eviction-priority policies (createpolicy) and the loads / stores that carry them.
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void st_l2_hint(int32_t *p, int32_t v, uint64_t pol) {
+    asm volatile("st.global.L2::cache_hint.b32 [%0], %1, %2;" ::"l"(p), "r"(v), "l"(pol) : "memory");
+}
+__device__ __forceinline__ int32_t ld_l2_hint(const int32_t *p, uint64_t pol) {
+    int32_t v;
+    asm volatile("ld.global.cg.L2::cache_hint.b32 %0, [%1], %2;" : "=r"(v) : "l"(p), "l"(pol) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ uint4 ldg_stream(const void *p) {
     uint4 v;
     asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"

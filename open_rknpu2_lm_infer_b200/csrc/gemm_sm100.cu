@@ -61,6 +61,11 @@ constexpr int EPI_WARPS = 8;
 constexpr int MAX_DYN_SMEM = 232448;        // 227 KB opt-in per block on sm_100
 constexpr int SMEM_RESERVE = 1024 + 1024;   // alignment slack + barriers
 constexpr int MAX_STAGES = 8;
+// Stream-K workspace: the contribution counters first, at a fixed place for every plan (they
+// must be zero before each launch, and the partial-sum buffers after them are overwritten
+// with plan-dependent layouts), room for SK_MAX_PAIRS pairs x 2 * EPI_WARPS sub-blocks.
+constexpr int SK_MAX_PAIRS = 256;
+constexpr size_t SK_CNT_BYTES = (size_t)SK_MAX_PAIRS * 2 * EPI_WARPS * sizeof(int);
 
 struct GemmArgs {
     const uint8_t *wq;     // W4 packed weights [Np][Kp/2] (read by the converter)
@@ -74,7 +79,92 @@ struct GemmArgs {
     int tok, stages, n_tok_tiles, num_tiles;
     uint32_t tmem_cols;
     unsigned *err;
+    int sk;              // 1: stream-K schedule, 0: whole tiles strided over the pairs
+    int sk_tiles;        // stream-K: the last sk_tiles tiles are split, the others whole
+    long long units;     // stream-K: (channel tile, k-block) iterations of one token tile
+                         // in the split region
+    int32_t *sk_ws;      // stream-K partial sums [pairs][left | right][tok][256]
+    int *sk_cnt;         // contributions per (slot, epilogue sub-block) [256][16], zero
+                         // between launches
 };
+
+// The work of one CTA pair, as a sequence of segments (tile t, k-blocks [kb0, kb1)).
+// Data-parallel: whole tiles cid, cid + ncl, ...  Stream-K: whole tiles first, then a share
+// of the split region.  The whole tiles are [0, T - sk_tiles), a whole number of waves,
+// strided over the pairs.  The split region is the last sk_tiles tiles: the pairs form one
+// group per token tile (pair cid serves token tile g = cid % G, G = n_tok_tiles, as the
+// i = cid / G-th of the group's Pg = ncl / G pairs); each group walks the U = (sk_tiles /
+// G) * nkb (channel tile, k-block) iterations of its token tile, pair i taking the
+// contiguous range [i U / Pg, (i + 1) U / Pg) cut at tile boundaries, so every pair gets
+// the same number of k-blocks (+-1) and the i-th pairs of all groups read the same weight
+// tiles at the same time (one DRAM read, the other groups hit L2).  The split region is
+// sized to absorb the imbalance of the last wave.  A split tile's segments are summed in a
+// global workspace (int32 sums are exact in any order, so the result does not depend on
+// which pair finishes first).  The split region comes last on purpose: measured on B200,
+// the loads that sum a split tile wait behind the TMA weight stream for tens of
+// microseconds while the main loops run, and are quick once it has ended.
+struct Sched {
+    long long u, end;  // split-region iterations still to walk
+    int t_dp, dp_end, step, nkb, ntt, g, base;
+    __device__ Sched(const GemmArgs &p, int cid, int ncl)
+        : t_dp(cid), step(ncl), nkb(p.nkb), ntt(p.n_tok_tiles) {
+        if (p.sk) {
+            const int pg = ncl / ntt, i = cid / ntt;
+            g = cid % ntt;
+            u = p.units * i / pg;
+            end = p.units * (i + 1) / pg;
+            base = dp_end = p.num_tiles - p.sk_tiles;
+        } else {
+            g = base = 0;
+            u = end = 0;
+            dp_end = p.num_tiles;
+        }
+    }
+    __device__ bool next(int &t, int &kb0, int &kb1) {
+        if (t_dp < dp_end) {
+            t = t_dp;
+            kb0 = 0;
+            kb1 = nkb;
+            t_dp += step;
+            return true;
+        }
+        if (u >= end) return false;
+        const int tc = (int)(u / nkb);
+        t = base + tc * ntt + g;
+        kb0 = (int)(u - (long long)tc * nkb);
+        const long long rem = end - u;
+        kb1 = rem < (long long)(nkb - kb0) ? kb0 + (int)rem : nkb;
+        u += kb1 - kb0;
+        return true;
+    }
+};
+
+// The same sequence one k-block at a time.
+struct Units {
+    Sched s;
+    int t = 0, kb = 0, k1 = 0;
+    bool live;
+    __device__ Units(const GemmArgs &p, int cid, int ncl) : s(p, cid, ncl) { live = s.next(t, kb, k1); }
+    __device__ void advance() {
+        if (++kb >= k1) live = s.next(t, kb, k1);
+    }
+};
+
+// Stream-K: the workspace slot of split tile t and how many segments it is cut into.  In
+// its token tile's group (Pg pairs, boundaries w_b = floor(b U / Pg)), the tile's range
+// [s0, e0) is cut by the boundaries b in [1, Pg) with s0 < w_b < e0; the slot is
+// g * Pg + (the first of them), distinct for every split tile.
+__device__ __forceinline__ void sk_split(const GemmArgs &p, int ncl, int t, int &slot, int &nseg) {
+    const int ntt = p.n_tok_tiles, tl = t - (p.num_tiles - p.sk_tiles);  // within the region
+    const int g = tl % ntt, tc = tl / ntt;
+    const long long pg = ncl / ntt;
+    const long long s0 = (long long)tc * p.nkb, e0 = s0 + p.nkb, U = p.units;
+    const long long bf = ((s0 + 1) * pg + U - 1) / U;  // first boundary with w_b > s0
+    long long bl = (e0 * pg + U - 1) / U - 1;          // last boundary with w_b < e0
+    if (bl > pg - 1) bl = pg - 1;
+    slot = g * (int)pg + (int)bf;
+    nseg = (int)(bl >= bf ? bl - bf + 1 : 0) + 1;
+}
 
 template <int BITS>
 constexpr int gemm_threads() { return (2 + EPI_WARPS + (BITS == 4 ? 4 : 0)) * 32; }
@@ -177,14 +267,21 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
             };
             // Weight tiles of the first stages do not depend on the preceding kernel:
             // issue them before waiting for it.
-            const int pre = ((int)cid < p.num_tiles) ? std::min(S, p.nkb) : 0;
-            for (int j = 0; j < pre; j++) load_weights(j, j, (int)cid / p.n_tok_tiles);
+            int pre = 0;
+            {
+                Sched sp(p, (int)cid, (int)ncl);
+                int t, kb0, kb1;
+                while (pre < S && sp.next(t, kb0, kb1))
+                    for (int kb = kb0; kb < kb1 && pre < S; kb++) load_weights(pre++, kb, t / p.n_tok_tiles);
+            }
             grid_dep_wait();
             uint32_t it = 0, s = 0, ph = 0;  // iteration, stage, stage phase
             bool ok = true;
-            for (int t = (int)cid; t < p.num_tiles && ok; t += (int)ncl) {
+            Sched sp(p, (int)cid, (int)ncl);
+            int t, kb0, kb1;
+            while (ok && sp.next(t, kb0, kb1)) {
                 const int tc = t / p.n_tok_tiles, tt = t % p.n_tok_tiles;
-                for (int kb = 0; kb < p.nkb; kb++, it++) {
+                for (int kb = kb0; kb < kb1; kb++, it++) {
                     if (it >= (uint32_t)pre) {
                         if (!(ok = mbar_wait(&empty[s], ph ^ 1, err, abort_flag))) break;
                         load_weights(s, kb, tc);
@@ -210,12 +307,14 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
             const uint32_t idesc = idesc_i8(2 * CH_CTA, tok, BITS == 8, true);
             uint32_t s = 0, ph = 0, local = 0;
             bool ok = true;
-            for (int t = (int)cid; t < p.num_tiles && ok; t += (int)ncl, local++) {
+            Sched sm(p, (int)cid, (int)ncl);
+            int t, kb0, kb1;
+            for (; ok && sm.next(t, kb0, kb1); local++) {
                 const int ab = local & 1;
                 if (!(ok = mbar_wait(&acce[ab], ((local >> 1) & 1) ^ 1, err, abort_flag))) break;
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(ab * tok);
-                for (int kb = 0; kb < p.nkb; kb++) {
+                for (int kb = kb0; kb < kb1; kb++) {
                     if (!(ok = mbar_wait(&full[s], ph, err, abort_flag))) break;
                     if (BITS == 4 && !(ok = mbar_wait(&afull[s], ph, err, abort_flag))) break;
                     tc_fence_after();
@@ -223,7 +322,7 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                     const uint64_t bdesc = smem_desc_sw128_k(sB + s * b_half);
 #pragma unroll
                     for (int k = 0; k < KB / 32; k++)
-                        mma_i8_ss_pair(d, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+                        mma_i8_ss_pair(d, adesc + 2 * k, bdesc + 2 * k, idesc, kb != kb0 || k != 0);
                     mma_commit_pair(&empty[s], 0x3);
                     if (++s == (uint32_t)S) { s = 0; ph ^= 1; }
                 }
@@ -240,10 +339,49 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
         grid_dep_wait();  // the activation scales / row sums come from the previous kernel
         const int q = warp & 3;                 // TMEM lane quadrant this warp may access
         const int colh = (warp - 2) >> 2;       // which half of the tok columns
-        const int cols = tok / 2;
+        const int cols = tok / 2;               // <= 128: at most 8 chunks of 16 columns
+        const int sub = (int)rank * EPI_WARPS + (warp - 2);  // this warp's part of a tile
+        const int chl = (int)rank * CH_CTA + q * 32 + lane;  // channel within the tile
         uint32_t local = 0;
         OutT *out = static_cast<OutT *>(p.out);
-        for (int t = (int)cid; t < p.num_tiles; t += (int)ncl, local++) {
+        // Activation scales (and W4 row sums) of this warp's columns, loaded once per tile:
+        // column c of the warp's range sits in lane c % 32 of register c / 32.
+        float sa_r[4];
+        int rs_r[4];
+        auto load_scales = [&](int tok_base) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int m = tok_base + i * 32 + lane;
+                const bool v = i * 32 + lane < cols && m < p.M;
+                sa_r[i] = v ? p.ascale[m] : 0.0f;
+                rs_r[i] = (BITS == 4 && v) ? p.rowsum[m] : 0;
+            }
+        };
+        // dequantise and store chunk cc (columns 16 cc .. 16 cc + 15 of the warp's range)
+        auto emit16 = [&](const uint32_t (&r)[16], int cc, int tok_base, int ch, bool chv,
+                          float sw) {
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const int src = (cc & 1) * 16 + j;
+                const float sa = __shfl_sync(0xffffffffu, sa_r[cc >> 1], src);
+                const int rs = __shfl_sync(0xffffffffu, rs_r[cc >> 1], src);
+                const int m = tok_base + cc * 16 + j;
+                if (chv && m < p.M) {
+                    int acc = (int)r[j];
+                    if (BITS == 4) acc -= 8 * rs;
+                    if constexpr (std::is_same<OutT, int32_t>::value) {
+                        out[(long long)m * p.ldc + ch] = acc;
+                    } else {
+                        const float y = __fmul_rn(__fmul_rn(__int2float_rn(acc), sa), sw);
+                        out[(long long)m * p.ldc + ch] = OutCvt<OutT>::from(y);
+                    }
+                }
+            }
+        };
+        const int pg = p.sk ? (int)ncl / p.n_tok_tiles : 1;  // stream-K pairs per group
+        Sched se(p, (int)cid, (int)ncl);
+        int t, kb0, kb1;
+        for (; se.next(t, kb0, kb1); local++) {
             const int tc = t / p.n_tok_tiles, tt = t % p.n_tok_tiles;
             const int ab = local & 1;
             // every lane waits (bounded); the warp leaves together if any lane gave up,
@@ -251,39 +389,104 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
             const bool okw = mbar_wait(&accf[ab], (local >> 1) & 1, err, abort_flag);
             if (!__all_sync(0xffffffffu, okw)) break;
             tc_fence_after();
-            const int ch = tc * CHT + (int)rank * CH_CTA + q * 32 + lane;
+            const int ch = tc * CHT + chl;
             const bool chv = ch < p.N;
-            const float sw = chv ? p.wscale[ch] : 0.0f;
+            const int tok_base = tt * tok + colh * cols;
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) +
                                    (uint32_t)(ab * tok + colh * cols);
-            for (int c = 0; c < cols / 16; c++) {
-                uint32_t r[16];
-                tmem_ld16(taddr + c * 16, r);
-                tmem_ld_wait();
-                const int tok0 = tt * tok + colh * cols + c * 16;
-                const bool lv = lane < 16 && tok0 + lane < p.M;
-                const float sa_l = lv ? p.ascale[tok0 + lane] : 0.0f;
-                const int rs_l = (BITS == 4 && lv) ? p.rowsum[tok0 + lane] : 0;
+            if (kb0 == 0 && kb1 == p.nkb) {
+                // the whole tile: dequantise from tensor memory
+                const float sw = chv ? p.wscale[ch] : 0.0f;
+                load_scales(tok_base);
 #pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    const float sa = __shfl_sync(0xffffffffu, sa_l, j);
-                    const int rs = __shfl_sync(0xffffffffu, rs_l, j);
-                    const int m = tok0 + j;
-                    if (chv && m < p.M) {
-                        int acc = (int)r[j];
-                        if (BITS == 4) acc -= 8 * rs;
-                        if constexpr (std::is_same<OutT, int32_t>::value) {
-                            out[(long long)m * p.ldc + ch] = acc;
-                        } else {
-                            const float y = __fmul_rn(__fmul_rn(__int2float_rn(acc), sa), sw);
-                            out[(long long)m * p.ldc + ch] = OutCvt<OutT>::from(y);
-                        }
-                    }
+                for (int cc = 0; cc < 8; cc++) {
+                    if (cc * 16 >= cols) break;
+                    uint32_t r[16];
+                    tmem_ld16(taddr + cc * 16, r);
+                    tmem_ld_wait();
+                    emit16(r, cc, tok_base, ch, chv, sw);
                 }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_remote(acce0 + 8u * ab);
+                continue;
+            }
+            // A segment of a split tile.  Its partial sums go to its own workspace buffer
+            // ([tok][256] int32, lanes = consecutive channels): the tile's first segment
+            // (it ends at the tile's first boundary b_f) to "left" of b_f, every other one
+            // to "right" of the pair boundary it starts at.  Then the contribution is
+            // counted; the warp that completes the count for its sub-block adds the tile's
+            // nseg buffers and finishes the sub-block.
+            int slot, nseg;
+            sk_split(p, (int)ncl, t, slot, nseg);  // slot = g * pg + b_f
+            const int g = (t - (p.num_tiles - p.sk_tiles)) % p.n_tok_tiles;
+            const int bstart = kb0 == 0 ? slot : g * pg + (int)cid / p.n_tok_tiles;
+            int32_t *mine = p.sk_ws + ((long long)(2 * bstart + (kb0 == 0 ? 0 : 1)) * tok) * CHT;
+            // the partial sums stay in L2 until the finishing warp reads them (the weight
+            // stream would otherwise push them out to DRAM, where their reads queue behind it)
+            const uint64_t keep = l2_policy_evict_last();
+#pragma unroll
+            for (int cc = 0; cc < 8; cc++) {
+                if (cc * 16 >= cols) break;
+                uint32_t r[16];
+                tmem_ld16(taddr + cc * 16, r);
+                tmem_ld_wait();
+                const int col0 = colh * cols + cc * 16;
+#pragma unroll
+                for (int j = 0; j < 16; j++)
+                    st_l2_hint(mine + (long long)(col0 + j) * CHT + chl, (int)r[j], keep);
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_remote(acce0 + 8u * ab);
+            if (lane == 0) mbar_arrive_remote(acce0 + 8u * ab);  // tensor memory is free
+            __threadfence();
+            __syncwarp();
+            int last = 0;
+            if (lane == 0) last = atomicAdd(p.sk_cnt + slot * (2 * EPI_WARPS) + sub, 1) == nseg - 1;
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (!last) continue;
+            __threadfence();
+            const float sw = chv ? p.wscale[ch] : 0.0f;
+            load_scales(tok_base);
+            // the tile's buffers: left of b_f, right of b_f .. b_f + nseg - 2.  Two chunks at
+            // a time, the loads of both first buffers issued together: under the main loops'
+            // traffic an L2 round trip costs microseconds, so the number of dependent
+            // round trips, not the bytes, sets the time of this pass.
+            const uint64_t drop = l2_policy_evict_first();
+            const int32_t *left = p.sk_ws + ((long long)(2 * slot) * tok) * CHT;
+            const int32_t *right0 = p.sk_ws + ((long long)(2 * slot + 1) * tok) * CHT;
+#pragma unroll
+            for (int cc = 0; cc < 8; cc += 2) {
+                if (cc * 16 >= cols) break;
+                const bool two = (cc + 1) * 16 < cols;
+                const int col0 = colh * cols + cc * 16;
+                uint32_t r[2][16], q2[2][16];
+#pragma unroll
+                for (int h = 0; h < 2; h++)
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        const long long off = (long long)(col0 + h * 16 + j) * CHT + chl;
+                        r[h][j] = (h == 0 || two) ? (uint32_t)ld_l2_hint(left + off, drop) : 0u;
+                        q2[h][j] = (h == 0 || two) ? (uint32_t)ld_l2_hint(right0 + off, drop) : 0u;
+                    }
+#pragma unroll
+                for (int h = 0; h < 2; h++)
+#pragma unroll
+                    for (int j = 0; j < 16; j++) r[h][j] += q2[h][j];
+                for (int sgi = 1; sgi < nseg - 1; sgi++) {  // tiles cut into three or more
+                    const int32_t *right = p.sk_ws + ((long long)(2 * (slot + sgi) + 1) * tok) * CHT;
+#pragma unroll
+                    for (int h = 0; h < 2; h++)
+#pragma unroll
+                        for (int j = 0; j < 16; j++)
+                            if (h == 0 || two)
+                                r[h][j] += (uint32_t)ld_l2_hint(
+                                    right + (long long)(col0 + h * 16 + j) * CHT + chl, drop);
+                }
+                emit16(r[0], cc, tok_base, ch, chv, sw);
+                if (two) emit16(r[1], cc + 1, tok_base, ch, chv, sw);
+            }
+            if (lane == 0) p.sk_cnt[slot * (2 * EPI_WARPS) + sub] = 0;
         }
     } else {
         // ------------------------------------------------------------ W4 converter
@@ -304,17 +507,17 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                 }
             };
             uint4 buf[W4_PREFETCH][4];
-            int ft = (int)cid, fkb = 0;  // prefetch stream position
+            Units fu(p, (int)cid, (int)ncl);  // prefetch stream position
 #pragma unroll
             for (int u = 0; u < W4_PREFETCH; u++) {
-                if (ft < p.num_tiles) {
-                    fetch(buf[u], ft, fkb);
-                    if (++fkb == p.nkb) { fkb = 0; ft += (int)ncl; }
+                if (fu.live) {
+                    fetch(buf[u], fu.t, fu.kb);
+                    fu.advance();
                 }
             }
             uint32_t s = 0, ph = 0;
-            int t = (int)cid, kb = 0;
-            bool live = t < p.num_tiles;
+            Units cu(p, (int)cid, (int)ncl);  // the iteration being unpacked
+            bool live = cu.live;
             while (live) {
 #pragma unroll
                 for (int u = 0; u < W4_PREFETCH; u++) {
@@ -337,9 +540,9 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                             *reinterpret_cast<uint4 *>(A + row * 128 + (((2 * cp + 1) ^ sw) << 4)) = c1;
                         }
                         // refill this register slot with the iteration W4_PREFETCH ahead
-                        if (ft < p.num_tiles) {
-                            fetch(buf[u], ft, fkb);
-                            if (++fkb == p.nkb) { fkb = 0; ft += (int)ncl; }
+                        if (fu.live) {
+                            fetch(buf[u], fu.t, fu.kb);
+                            fu.advance();
                         }
                         // every writer makes its stores visible to the async proxy and
                         // arrives locally; one thread collects the 128 arrivals (bounded) and
@@ -351,11 +554,8 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                             else mbar_arrive_remote(afull0 + 8u * s);
                         }
                         if (++s == (uint32_t)S) { s = 0; ph ^= 1; }
-                        if (++kb == p.nkb) {
-                            kb = 0;
-                            t += (int)ncl;
-                            live = t < p.num_tiles;
-                        }
+                        cu.advance();
+                        if (!cu.live) live = false;
                     }
                 }
             }
@@ -433,7 +633,7 @@ int pair_capacity_t() {
 // both available); the persistent grid is sized to it so every pair is resident.
 int gemm_pair_capacity(int bits) { return bits == 8 ? pair_capacity_t<8>() : pair_capacity_t<4>(); }
 
-GemmPlan plan_gemm(const WeightView &w, int rows, int max_pairs) {
+GemmPlan plan_gemm(const WeightView &w, int rows, int max_pairs, bool allow_sk) {
     GemmPlan plan{};
     const int tiles_m = std::max(1, (rows + 255) / 256);
     int tok = (rows + tiles_m - 1) / tiles_m;
@@ -447,13 +647,51 @@ GemmPlan plan_gemm(const WeightView &w, int rows, int max_pairs) {
     plan.smem_bytes = std::max(stages * stage_bytes + fixed, 120 * 1024);
     const int n_tok_tiles = (rows + tok - 1) / tok;
     plan.tiles = ((w.Np + CHT - 1) / CHT) * n_tok_tiles;
-    plan.grid = 2 * std::min(plan.tiles, std::max(1, max_pairs));
+    // Whole tiles strided over the pairs.  With allow_sk, stream-K where that leaves much of
+    // the GPU idle (fewer tiles than pairs, or a mostly empty last wave: cfg4 at M=512 runs
+    // 224 tiles on 74 pairs in 4 waves for 3.03 waves of work), on (nearly) every resident
+    // pair -- a multiple of the token tiles, one group per token tile -- provided the k-loop
+    // is long enough that cutting it costs little.  Measured on B200 it balances the main
+    // loops as intended (every pair's last MMA within ~1 us of the others) but the pass
+    // that finishes split tiles is bound by the epilogue's output stores (one 16-token
+    // chunk of a warp's fp16 stores takes ~1.3 us while the main loops run, ~3.5 us when
+    // every pair finishes at once), so it loses to whole tiles on every shape tried
+    // (cfg4 M=512: 122 vs 108 us per call) and is off unless asked for.
+    const int maxp = std::max(1, max_pairs);
+    const int dp_pairs = std::min(plan.tiles, maxp);
+    const long long waves = (plan.tiles + dp_pairs - 1) / dp_pairs;
+    const int nkb = w.Kp / KB;
+    const long long ch_tiles = (w.Np + CHT - 1) / CHT;
+    const long long group = std::min<long long>(maxp / n_tok_tiles, ch_tiles * nkb);
+    plan.sk = 0;
+    plan.sk_tiles = 0;
+    if (allow_sk && group >= 1 && nkb >= 8) {
+        const long long sk_pairs = group * n_tok_tiles;
+        // stream-K's balanced work vs the data-parallel waves, both on the whole GPU
+        const double dp_eff = (double)plan.tiles / ((double)waves * maxp);
+        const double sk_eff = (double)sk_pairs / maxp;
+        if (dp_eff < 0.9 && sk_eff > dp_eff + 0.05) {
+            plan.sk = 1;
+            // whole waves of whole tiles after the split region (keep at least one wave's
+            // worth of tiles, and the last partial wave, split)
+            const long long whole = std::max<long long>(0, plan.tiles / sk_pairs - 1);
+            plan.sk_tiles = (int)(plan.tiles - whole * sk_pairs);
+        }
+    }
+    const int pairs = plan.sk ? (int)(group * n_tok_tiles) : dp_pairs;
+    plan.grid = 2 * pairs;
     return plan;
+}
+
+size_t gemm_sk_bytes(const GemmPlan &plan) {
+    if (!plan.sk) return 0;
+    const size_t pairs = (size_t)plan.grid / 2;
+    return SK_CNT_BYTES + 2 * pairs * (size_t)plan.tok * CHT * sizeof(int32_t);
 }
 
 cudaError_t launch_gemm(const WeightView &w, const CUtensorMap &wmap, const ActView &a,
                         const CUtensorMap &amap, const GemmPlan &plan, int rows, void *out,
-                        int out_type, long long ldc, unsigned *err, bool pdl,
+                        int out_type, long long ldc, unsigned *err, void *sk_ws, bool pdl,
                         cudaStream_t stream) {
     GemmArgs args{};
     args.wq = w.w;
@@ -474,6 +712,13 @@ cudaError_t launch_gemm(const WeightView &w, const CUtensorMap &wmap, const ActV
     while (cols < (uint32_t)(2 * plan.tok)) cols <<= 1;
     args.tmem_cols = cols;
     args.err = err;
+    args.sk_tiles = plan.sk_tiles;
+    args.units = (long long)(plan.sk_tiles / args.n_tok_tiles) * args.nkb;
+    args.sk = plan.sk && sk_ws && plan.grid / 2 <= SK_MAX_PAIRS ? 1 : 0;
+    if (args.sk) {
+        args.sk_cnt = static_cast<int *>(sk_ws);
+        args.sk_ws = reinterpret_cast<int32_t *>(static_cast<char *>(sk_ws) + SK_CNT_BYTES);
+    }
     if (w.bits == 8) {
         if (out_type == kF16) return launch_t<8, __half>(wmap, amap, args, plan, pdl, stream);
         if (out_type == kF32) return launch_t<8, float>(wmap, amap, args, plan, pdl, stream);

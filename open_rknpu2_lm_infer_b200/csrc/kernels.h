@@ -69,15 +69,25 @@ struct GemmPlan {
     int smem_bytes; // dynamic shared memory
     int grid;       // persistent CTAs
     int tiles;
+    int sk;         // 1: stream-K (every pair the same number of k-blocks, split tiles
+                    //    summed in a workspace), 0: whole tiles strided over the pairs
+    int sk_tiles;   // stream-K: the split region, the last sk_tiles tiles
 };
-// max_pairs: gemm_pair_capacity() of the device (CTA pairs resident at once).
-GemmPlan plan_gemm(const WeightView &w, int rows, int max_pairs);
+// max_pairs: gemm_pair_capacity() of the device (CTA pairs resident at once); allow_sk: the
+// plan may choose the stream-K schedule (QLINEAR_BACKEND_GEMM_STREAM_K).
+GemmPlan plan_gemm(const WeightView &w, int rows, int max_pairs, bool allow_sk);
 int gemm_pair_capacity(int bits);
+// Bytes of the stream-K workspace a plan needs (0 without stream-K): partial-sum buffers
+// (no initial value needed) and per-tile contribution counters, which must be zero before a
+// launch.  The caller zero-fills it once; every launch leaves the counters zero again
+// (unless a launch gave up on a timeout).
+size_t gemm_sk_bytes(const GemmPlan &plan);
 // pdl: launch with programmatic stream serialization (the kernel waits with
-// griddepcontrol.wait before reading the activation codes / scales).
+// griddepcontrol.wait before reading the activation codes / scales).  sk_ws: the zeroed
+// stream-K workspace of gemm_sk_bytes(plan) bytes (ignored without stream-K).
 cudaError_t launch_gemm(const WeightView &w, const CUtensorMap &wmap, const ActView &a,
                         const CUtensorMap &amap, const GemmPlan &plan, int rows, void *out,
-                        int out_type, long long ldc, unsigned *err, bool pdl,
+                        int out_type, long long ldc, unsigned *err, void *sk_ws, bool pdl,
                         cudaStream_t stream);
 
 // SwiGLU over an f32 [rows][N] buffer: out[m][j] = silu(y[m][j]) * y[m][N/2 + j].

@@ -46,6 +46,10 @@ struct qlinear_backend {
     // f32 gate/up scratch for SwiGLU through the GEMM
     float *d_y = nullptr;
     size_t y_elems = 0;
+    // stream-K partial sums and contribution counters of the GEMM (counters zero between
+    // launches)
+    void *d_sk = nullptr;
+    size_t sk_bytes = 0;
     // host path staging
     void *d_in = nullptr, *d_out = nullptr;
     size_t d_in_bytes = 0, d_out_bytes = 0;
@@ -57,7 +61,7 @@ struct qlinear_backend {
     int max_kp = 0, max_n = 0;
     int prepared_rows = 0;
     unsigned long long launches = 0;
-    unsigned long long gemv_calls = 0, gemm_calls = 0;
+    unsigned long long gemv_calls = 0, gemm_calls = 0, gemm_stream_k_calls = 0;
     std::map<std::tuple<const void *, int, int, size_t>, CUtensorMap> amaps;
     // per-kernel device timing (qlinear_backend_profile)
     bool profiling = false;
@@ -205,6 +209,25 @@ int ensure_dev(void **p, size_t *cap, size_t need) {
     return QLINEAR_OK;
 }
 
+// The stream-K workspace: grown on demand, zero-filled when (re)allocated; the GEMM leaves
+// its counters zero after every launch that completes.
+int ensure_sk(qlinear_backend *b, size_t need) {
+    if (need <= b->sk_bytes) return QLINEAR_OK;
+    cudaFree(b->d_sk);
+    b->d_sk = nullptr;
+    b->sk_bytes = 0;
+    need = (need + 4095) / 4096 * 4096;
+    QL_TRY(cudaMalloc(&b->d_sk, need));
+    QL_TRY(cudaMemset(b->d_sk, 0, need));
+    b->sk_bytes = need;
+    return QLINEAR_OK;
+}
+
+// After a device-side timeout a GEMM may have left contribution counters behind.
+void reset_after_timeout(qlinear_backend *b) {
+    if (b->d_sk) cudaMemset(b->d_sk, 0, b->sk_bytes);
+}
+
 int ensure_host(void **p, size_t *cap, size_t need) {
     if (need <= *cap) return QLINEAR_OK;
     cudaFreeHost(*p);
@@ -309,20 +332,22 @@ int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_
     const bool use8 = w->d_w8 != nullptr;
     const WeightView &gv = use8 ? w->view8 : v;
     const CUtensorMap &gmap = use8 ? w->wmap8 : w->wmap;
-    const GemmPlan plan = plan_gemm(gv, rows, pairs);
+    const GemmPlan plan = plan_gemm(gv, rows, pairs, (b->flags & QLINEAR_BACKEND_GEMM_STREAM_K) != 0);
+    if ((st = ensure_sk(b, gemm_sk_bytes(plan)))) return st;
+    if (plan.sk) b->gemm_stream_k_calls++;
     const CUtensorMap *amap = nullptr;
     st = get_amap(b, v.Kp, plan.tok, &amap);
     if (st) return st;
     if (!swiglu) {
-        QL_TRY(launch_gemm(gv, gmap, av, *amap, plan, rows, c_dev, c_type, ldc, b->d_err, true,
-                           stream));
+        QL_TRY(launch_gemm(gv, gmap, av, *amap, plan, rows, c_dev, c_type, ldc, b->d_err, b->d_sk,
+                           true, stream));
         b->launches++;
     } else {
         st = ensure_dev(reinterpret_cast<void **>(&b->d_y), &b->y_elems,
                         (size_t)rows * v.N * sizeof(float));
         if (st) return st;
-        QL_TRY(launch_gemm(gv, gmap, av, *amap, plan, rows, b->d_y, kF32, v.N, b->d_err, true,
-                           stream));
+        QL_TRY(launch_gemm(gv, gmap, av, *amap, plan, rows, b->d_y, kF32, v.N, b->d_err, b->d_sk,
+                           true, stream));
         QL_TRY(launch_swiglu(b->d_y, rows, v.N, c_dev, c_type, ldc, stream));
         b->launches += 2;
     }
@@ -440,7 +465,8 @@ qlinear_backend *qlinear_backend_create(const qlinear_backend_config *cfg) {
     if (!cfg) cfg = &def;
     if (cfg->round_mode != QLINEAR_ROUND_AWAY && cfg->round_mode != QLINEAR_ROUND_EVEN)
         return fail(QLINEAR_ERR_PARAM), nullptr;
-    if (cfg->max_rows < 0 || (cfg->flags & ~QLINEAR_BACKEND_W4_PACKED_ONLY))
+    if (cfg->max_rows < 0 ||
+        (cfg->flags & ~(QLINEAR_BACKEND_W4_PACKED_ONLY | QLINEAR_BACKEND_GEMM_STREAM_K)))
         return fail(QLINEAR_ERR_PARAM), nullptr;
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || cfg->device < 0 || cfg->device >= ndev)
@@ -476,6 +502,7 @@ void qlinear_backend_free(qlinear_backend *b) {
     cudaFree(b->d_ascale);
     cudaFree(b->d_rowsum);
     cudaFree(b->d_y);
+    cudaFree(b->d_sk);
     cudaFree(b->d_in);
     cudaFree(b->d_out);
     cudaFree(b->d_err);
@@ -587,6 +614,7 @@ static int run_host(qlinear_backend *b, const qlinear_weights *w, const float *a
     if (*b->h_err) {
         cudaMemsetAsync(b->d_err, 0, sizeof(unsigned), b->stream);
         cudaStreamSynchronize(b->stream);
+        reset_after_timeout(b);
         return QLINEAR_ERR_TIMEOUT;
     }
     if (ldc == width) {
@@ -675,6 +703,7 @@ int qlinear_backend_check(qlinear_backend *b, void *stream) {
     QL_TRY(cudaMemcpy(b->h_err, b->d_err, sizeof(unsigned), cudaMemcpyDeviceToHost));
     if (*b->h_err) {
         QL_TRY(cudaMemset(b->d_err, 0, sizeof(unsigned)));
+        reset_after_timeout(b);
         return QLINEAR_ERR_TIMEOUT;
     }
     return QLINEAR_OK;
@@ -692,12 +721,13 @@ int qlinear_backend_stats(const qlinear_backend *b, char *buf, size_t len) {
         "\"tune_cache_misses\": 0, \"tune_calls\": 0, \"strategy_fallbacks\": 0, "
         "\"strategy_fallback_calls\": 0, \"weight_reload_calls\": 0, \"round_mode\": \"%s\", "
         "\"prepared_rows\": %d, \"kernel_launches\": %llu, \"gemv_calls\": %llu, "
-        "\"gemm_calls\": %llu, \"gemm_pairs_resident\": [%d, %d]}",
+        "\"gemm_calls\": %llu, \"gemm_stream_k_calls\": %llu, "
+        "\"gemm_pairs_resident\": [%d, %d]}",
         b->device, b->num_sms, b->loaded_w4, b->loaded_w8, (unsigned long long)b->weight_bytes,
         (unsigned long long)ws, b->ws_bytes ? 1 : 0,
         (unsigned long long)(b->h_in_bytes + b->h_out_bytes),
         b->round_mode == QLINEAR_ROUND_AWAY ? "away" : "even", b->prepared_rows, b->launches,
-        b->gemv_calls, b->gemm_calls, b->gemm_pairs[0], b->gemm_pairs[1]);
+        b->gemv_calls, b->gemm_calls, b->gemm_stream_k_calls, b->gemm_pairs[0], b->gemm_pairs[1]);
     if (n < 0) return QLINEAR_ERR_PARAM;
     if (buf && len) {
         std::strncpy(buf, tmp, len - 1);

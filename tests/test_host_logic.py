@@ -128,3 +128,83 @@ def test_workload_distributions():
     bits = W.layer_bits()
     frac = np.mean([b == 4 for row in bits for b in row])
     assert 0.6 < frac < 0.8
+
+
+# ---------------------------------------------------------------------------------------
+# Stream-K schedule of the GEMM (csrc/gemm_sm100.cu: plan_gemm, Sched, sk_split), restated
+# with the same integer formulas: a split region of sk_tiles tiles walked by groups of pairs
+# (one group per token tile), then whole tiles strided over the pairs.  Every (tile,
+# k-block) is covered exactly once, every pair gets the same work (+-1 k-block), the segment
+# count of a split tile equals sk_split's nseg, and split tiles get distinct workspace slots.
+
+def _sk_plan(ch_tiles, ntt, nkb, maxp):
+    tiles = ch_tiles * ntt
+    group = min(maxp // ntt, ch_tiles * nkb)
+    P = group * ntt
+    whole = max(0, tiles // P - 1)
+    return P, tiles - whole * P
+
+
+def _sk_segments(ch_tiles, ntt, nkb, P, sk_tiles, cid):
+    base = ch_tiles * ntt - sk_tiles  # whole tiles first, then the split region
+    t = cid
+    while t < base:
+        yield t, 0, nkb
+        t += P
+    pg, i, g = P // ntt, cid // ntt, cid % ntt
+    units = (sk_tiles // ntt) * nkb
+    u, end = units * i // pg, units * (i + 1) // pg
+    while u < end:
+        tc = u // nkb
+        kb0 = u - tc * nkb
+        kb1 = kb0 + (end - u) if end - u < nkb - kb0 else nkb
+        yield base + tc * ntt + g, kb0, kb1
+        u += kb1 - kb0
+
+
+def _sk_split(t, sk_tiles, ntt, nkb, P, tiles):
+    t -= tiles - sk_tiles
+    g, tc, pg = t % ntt, t // ntt, P // ntt
+    units = (sk_tiles // ntt) * nkb
+    s0, e0 = tc * nkb, tc * nkb + nkb
+    bf = ((s0 + 1) * pg + units - 1) // units
+    bl = min((e0 * pg + units - 1) // units - 1, pg - 1)
+    return g * pg + bf, (bl - bf + 1 if bl >= bf else 0) + 1
+
+
+def test_stream_k_schedule_covers_every_iteration_once():
+    import random
+    rng = random.Random(5)
+    cases = [(112, 2, 64, 74), (38, 2, 20, 74), (10, 1, 8, 74), (3, 1, 8, 24), (1, 1, 8, 8),
+             (112, 4, 64, 74), (112, 3, 64, 74), (14, 2, 64, 74), (38, 1, 20, 74)]
+    cases += [(rng.randint(1, 200), rng.randint(1, 6), rng.randint(8, 80), rng.randint(1, 74))
+              for _ in range(3000)]
+    for ch_tiles, ntt, nkb, maxp in cases:
+        if maxp // ntt < 1:
+            continue
+        P, sk_tiles = _sk_plan(ch_tiles, ntt, nkb, maxp)
+        tiles = ch_tiles * ntt
+        assert sk_tiles % ntt == 0 and (tiles - sk_tiles) % P == 0
+        seen, work = {}, []
+        for cid in range(P):
+            segs = list(_sk_segments(ch_tiles, ntt, nkb, P, sk_tiles, cid))
+            assert segs, (ch_tiles, ntt, nkb, P, cid)      # no pair is idle
+            work.append(sum(b - a for _, a, b in segs))
+            for t, kb0, kb1 in segs:
+                assert 0 <= t < tiles and 0 <= kb0 < kb1 <= nkb
+                assert t < tiles - sk_tiles or (t - (tiles - sk_tiles)) % ntt == cid % ntt
+                seen.setdefault(t, []).append((kb0, kb1))
+        assert max(work) - min(work) <= 1
+        slots = set()
+        for t in range(tiles):
+            segs = sorted(seen[t])
+            assert segs[0][0] == 0 and segs[-1][1] == nkb
+            assert all(a[1] == b[0] for a, b in zip(segs, segs[1:]))
+            if t < tiles - sk_tiles:
+                assert len(segs) == 1
+                continue
+            slot, nseg = _sk_split(t, sk_tiles, ntt, nkb, P, tiles)
+            assert nseg == len(segs), (ch_tiles, ntt, nkb, P, t)
+            if nseg > 1:
+                assert 0 <= slot < P and slot not in slots
+                slots.add(slot)
