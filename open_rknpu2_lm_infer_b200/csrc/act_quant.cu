@@ -103,9 +103,6 @@ __global__ void __launch_bounds__(kThreads) act_quant_vec_kernel(
     int8_t *cr = codes + m * (long long)Kp;
     const int nchunks = K / V;
 
-    // Let a dependent kernel launched with programmatic stream serialization start its
-    // prologue now; it waits (griddepcontrol.wait) before reading what this kernel writes.
-    asm volatile("griddepcontrol.launch_dependents;");
     const uint4 *xv = reinterpret_cast<const uint4 *>(xr);
     uint4 raw[kCache];
     float amax = 0.0f;
@@ -163,6 +160,12 @@ __global__ void __launch_bounds__(kThreads) act_quant_vec_kernel(
         scales[m] = scale;
         if (rowsums) rowsums[m] = sum;
     }
+    // Let a dependent kernel launched with programmatic stream serialization (the GEMM /
+    // GEMV) launch once every row's CTA got here; it waits (griddepcontrol.wait) before
+    // reading what this kernel wrote.  Triggering at the end rather than the start keeps
+    // the dependent's CTAs (a GEMM CTA holds most of an SM) from crowding out the rows
+    // still to be quantised.
+    asm volatile("griddepcontrol.launch_dependents;");
 }
 
 // Scalar path for any K / alignment (re-reads the row for the second pass).
@@ -172,7 +175,6 @@ __global__ void __launch_bounds__(kThreads) act_quant_scalar_kernel(
     int8_t *__restrict__ codes, float *__restrict__ scales, int32_t *__restrict__ rowsums) {
     __shared__ float redf[32];
     __shared__ int redi[32];
-    asm volatile("griddepcontrol.launch_dependents;");
     const long long m = blockIdx.x;
     const T *xr = x + m * ldx;
     int8_t *cr = codes + m * (long long)Kp;
@@ -193,6 +195,7 @@ __global__ void __launch_bounds__(kThreads) act_quant_scalar_kernel(
         scales[m] = scale;
         if (rowsums) rowsums[m] = sum;
     }
+    asm volatile("griddepcontrol.launch_dependents;");
 }
 
 template <typename T>

@@ -11,6 +11,7 @@
 // ragged tiles), no tuning (one static dispatch), run_swiglu supported for W4 and W8.
 #include "../../include/qlinear.h"
 #include "common.cuh"
+#include "host_pool.h"
 #include "kernels.h"
 
 #include <cudaTypedefs.h>
@@ -19,8 +20,10 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <memory>
 #include <mutex>
 #include <new>
+#include <thread>
 #include <string>
 #include <tuple>
 #include <vector>
@@ -55,6 +58,8 @@ struct qlinear_backend {
     size_t d_in_bytes = 0, d_out_bytes = 0;
     void *h_in = nullptr, *h_out = nullptr;
     size_t h_in_bytes = 0, h_out_bytes = 0;
+    std::unique_ptr<HostPool> pool;         // host copies of the f32 host path
+    std::vector<cudaEvent_t> chunk_events;  // one per output chunk in flight
     // bookkeeping (Backend::stats)
     int loaded_w4 = 0, loaded_w8 = 0;
     uint64_t weight_bytes = 0;
@@ -509,6 +514,8 @@ void qlinear_backend_free(qlinear_backend *b) {
     cudaFreeHost(b->h_in);
     cudaFreeHost(b->h_out);
     cudaFreeHost(b->h_err);
+    for (auto e : b->chunk_events) cudaEventDestroy(e);
+    b->pool.reset();
     for (auto &e : b->prof_events)
         for (auto x : e) cudaEventDestroy(x);
     if (b->stream) cudaStreamDestroy(b->stream);
@@ -603,26 +610,57 @@ static int run_host(qlinear_backend *b, const qlinear_weights *w, const float *a
         (st = ensure_dev(&b->d_in, &b->d_in_bytes, in_bytes)) ||
         (st = ensure_dev(&b->d_out, &b->d_out_bytes, out_bytes)))
         return st;
-    std::memcpy(b->h_in, a_host, in_bytes);
-    QL_TRY(cudaMemcpyAsync(b->d_in, b->h_in, in_bytes, cudaMemcpyHostToDevice, b->stream));
+    if (!b->pool) {
+        const unsigned hw = std::thread::hardware_concurrency();
+        b->pool.reset(new (std::nothrow) HostPool((int)std::min(16u, std::max(1u, hw)) - 1));
+        if (!b->pool) return QLINEAR_ERR_ALLOC;
+    }
+    HostPool &pool = *b->pool;
+    // Input: row chunks of ~2 MB copied into pinned staging by the pool, each sent as soon
+    // as it is staged, so the next chunk's copy overlaps the previous chunk's transfer.
+    const size_t in_row = (size_t)v.K * sizeof(float), out_row = (size_t)width * sizeof(float);
+    char *h_in = static_cast<char *>(b->h_in), *d_in = static_cast<char *>(b->d_in);
+    const int in_chunk = (int)std::max<size_t>(1, (2u << 20) / in_row);
+    for (int r0 = 0; r0 < rows; r0 += in_chunk) {
+        const int n = std::min(in_chunk, rows - r0);
+        pool.copy_rows(h_in + r0 * in_row, in_row, a_host + (size_t)r0 * v.K, in_row, n, in_row);
+        QL_TRY(cudaMemcpyAsync(d_in + r0 * in_row, h_in + r0 * in_row, n * in_row,
+                               cudaMemcpyHostToDevice, b->stream));
+    }
     st = run_device_impl(b, w, b->d_in, QLINEAR_F32, b->d_out, QLINEAR_F32, width, rows, flags,
                          b->stream);
     if (st) return st;
-    QL_TRY(cudaMemcpyAsync(b->h_out, b->d_out, out_bytes, cudaMemcpyDeviceToHost, b->stream));
+    // Output: row chunks of ~4 MB, each transfer followed by an event; each chunk is copied
+    // to the caller's rows (stride ldc) while the next ones are still in transit.
+    int out_chunk = (int)std::max<size_t>(1, (4u << 20) / out_row);
+    const int kMaxChunks = 64;
+    out_chunk = std::max(out_chunk, (rows + kMaxChunks - 1) / kMaxChunks);
+    const int nchunks = (rows + out_chunk - 1) / out_chunk;
+    while ((int)b->chunk_events.size() < nchunks) {
+        cudaEvent_t e;
+        QL_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        b->chunk_events.push_back(e);
+    }
+    char *h_out = static_cast<char *>(b->h_out), *d_out = static_cast<char *>(b->d_out);
+    for (int i = 0; i < nchunks; i++) {
+        const int r0 = i * out_chunk, n = std::min(out_chunk, rows - r0);
+        QL_TRY(cudaMemcpyAsync(h_out + r0 * out_row, d_out + r0 * out_row, n * out_row,
+                               cudaMemcpyDeviceToHost, b->stream));
+        QL_TRY(cudaEventRecord(b->chunk_events[i], b->stream));
+    }
     QL_TRY(cudaMemcpyAsync(b->h_err, b->d_err, sizeof(unsigned), cudaMemcpyDeviceToHost, b->stream));
+    for (int i = 0; i < nchunks; i++) {
+        const int r0 = i * out_chunk, n = std::min(out_chunk, rows - r0);
+        QL_TRY(cudaEventSynchronize(b->chunk_events[i]));
+        pool.copy_rows(c_host + (size_t)r0 * ldc, (size_t)ldc * sizeof(float), h_out + r0 * out_row,
+                       out_row, n, out_row);
+    }
     QL_TRY(cudaStreamSynchronize(b->stream));
     if (*b->h_err) {
         cudaMemsetAsync(b->d_err, 0, sizeof(unsigned), b->stream);
         cudaStreamSynchronize(b->stream);
         reset_after_timeout(b);
         return QLINEAR_ERR_TIMEOUT;
-    }
-    if (ldc == width) {
-        std::memcpy(c_host, b->h_out, out_bytes);
-    } else {
-        const float *src = static_cast<const float *>(b->h_out);
-        for (int r = 0; r < rows; r++)
-            std::memcpy(c_host + (size_t)r * ldc, src + (size_t)r * width, (size_t)width * sizeof(float));
     }
     return QLINEAR_OK;
 }
