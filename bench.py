@@ -62,6 +62,9 @@ def parse():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg4")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="target CPU time of the oracle baseline sample")
+    ap.add_argument("--exchange", choices=["gather", "fused"], default="gather",
+                    help="split-N output exchange at N>1: NCCL all-gather + column assembly, "
+                         "or the kernels' epilogues storing into every rank's buffer")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
@@ -249,22 +252,35 @@ def run_ours(args, rank, world, local_rank):
     backend = Backend(device=local_rank)
     codes = W.weight_codes(bits, k, n)
     scales = W.weight_scales(n)
-    lin = backend.load_shard(QuantMatrix(bits, k, n, codes, scales), n0, n0 + ns)
-    del codes
+    qm = QuantMatrix(bits, k, n, codes, scales)
+    sharded = None
+    fused = args.exchange == "fused"
+    if world > 1:
+        # split-N; the [M][N] output put together on every rank either by an NCCL all-gather
+        # of the slabs + column assembly, or (fused) by the kernels' epilogues storing each
+        # rank's columns into every rank's buffer over NVLink
+        from open_rknpu2_lm_infer_b200.sharded import ShardedLinear
+        sharded = ShardedLinear(backend, qm, fused_exchange=fused, max_rows=m)
+        lin = sharded.linear
+    else:
+        lin = backend.load_shard(qm, n0, n0 + ns)
+    del codes, qm
     backend.prepare(m)
     x_host = W.activations(m, k)
     x = torch.from_numpy(x_host).to(dev)
-    y_local = torch.empty((m, ns), dtype=torch.float16, device=dev)
-    y_gather = torch.empty((world * m, ns), dtype=torch.float16, device=dev) if world > 1 else None
-    y_full = torch.empty((m, n), dtype=torch.float16, device=dev) if world > 1 else y_local
+    y_local = torch.empty((m, ns), dtype=torch.float16, device=dev) if world == 1 else None
+    y_full = torch.empty((m, n), dtype=torch.float16, device=dev) if world > 1 and not fused \
+        else None
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev).cuda_stream
 
     def step():
-        lin.run_device(x, y_local, m, stream=stream)
-        if world > 1:
-            dist.all_gather_into_tensor(y_gather, y_local)
-            backend.interleave_columns(y_gather, y_full, world, m, ns, 2, stream=stream)
+        if world > 1 and fused:
+            sharded.run_exchange(x, m, stream=stream)
+        elif world > 1:
+            sharded.run_device(x, y_full, m, stream=stream)
+        else:
+            lin.run_device(x, y_local, m, stream=stream)
 
     def barrier():
         if world > 1:
@@ -350,13 +366,26 @@ def run_ours(args, rank, world, local_rank):
         "warmup": args.warmup, "ms_per_step": mean_step * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
         "config": {"workload": desc, "M": m, "K": k, "N": n, "bits": bits,
-                   "parallelism": f"split-N x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+                   "parallelism": f"split-N x{world}" + (
+                       "" if world == 1 else
+                       " + output exchange fused into the kernels (NVLink peer stores)"
+                       if fused else " + NCCL all-gather"),
                    "l2": "flushed (256 MiB write) between timed steps, outside the timed region",
                    "inputs": "fp16 N(0,1) with 1% x20 outlier channels, seed 42"},
         "roofline": roofline,
         "gpu_launches": int(launches_timed),
         "clocks": clocks,
     }
+    # The split-N output exchange bounds the end-to-end scaling of this layer; report the
+    # kernels' time beside the whole step.
+    compute_s = (main_s + quant_s) / max(calls, 1)
+    line["compute_only"] = {
+        "value": ops / compute_s / 1e12, "unit": "TOPS", "per_step_us": compute_s * 1e6,
+        "exchange_us": max(0.0, mean_step - compute_s) * 1e6,
+        "note": "act-quant + GEMM device time per step (max over ranks; with the fused "
+                "exchange the GEMM includes its peer stores), without the rest of the output "
+                "exchange (all-gather + assembly, or the completion all-reduce) that `value` "
+                "includes"}
 
     # decode half of the metric: W8A8 K2560 N9728 M=1 (HBM-bound GEMV)
     if not args.no_decode:
@@ -365,7 +394,7 @@ def run_ours(args, rank, world, local_rank):
     # end to end through the public C ABI with host buffers
     if not args.no_e2e:
         line["e2e"] = e2e_measure(backend, lin, torch, dist, dev, args, world, m, k, n, ns,
-                                  x_host, y_gather)
+                                  x_host, sharded)
 
     if rank == 0 and world == 1 and not args.no_cpu:
         ops_s, rows, dt, threads = oracle_sample(bits, k, n, m, args.cpu_seconds)
@@ -377,7 +406,10 @@ def run_ours(args, rank, world, local_rank):
     line["gpu_launches"] = int(launches_timed)
     if rank == 0:
         print(json.dumps(line), flush=True)
-    lin.close()
+    if sharded is not None:
+        sharded.close()  # collective: unmaps the peers' buffers, frees this rank's
+    else:
+        lin.close()
     backend.close()
 
 
@@ -441,10 +473,10 @@ def decode_measure(backend, torch, dev, args, world):
                                   "back-to-back calls, CUDA events"}}
 
 
-def e2e_measure(backend, lin, torch, dist, dev, args, world, m, k, n, ns, x_host, y_gather):
+def e2e_measure(backend, lin, torch, dist, dev, args, world, m, k, n, ns, x_host, sharded):
     """Same metric through the public API with host buffers: H2D of the f32 input, the
-    path, (all-gather), D2H of the f32 output, every step; wall-clock between host
-    synchronisations, max over ranks."""
+    path (with the fused output exchange at N>1), D2H of the f32 output, every step;
+    wall-clock between host synchronisations, max over ranks."""
     xin = np.ascontiguousarray(x_host.astype(np.float32))
     steps = max(3, min(args.steps, 10))
     if world == 1:
@@ -462,17 +494,21 @@ def e2e_measure(backend, lin, torch, dist, dev, args, world, m, k, n, ns, x_host
         pin_in = torch.from_numpy(xin).pin_memory()
         pin_out = torch.empty((m, n), dtype=torch.float32).pin_memory()
         xd = torch.empty((m, k), dtype=torch.float32, device=dev)
-        yl = torch.empty((m, ns), dtype=torch.float32, device=dev)
-        yg = torch.empty((world * m, ns), dtype=torch.float32, device=dev)
-        yf = torch.empty((m, n), dtype=torch.float32, device=dev)
+        fused = args.exchange == "fused"
+        if fused:
+            sharded.add_exchange(m, torch.float32)  # the host API's type
+        else:
+            yf = torch.empty((m, n), dtype=torch.float32, device=dev)
         stream = torch.cuda.current_stream(dev).cuda_stream
 
         def one():
             xd.copy_(pin_in, non_blocking=True)
-            lin.run_device(xd, yl, m, stream=stream)
-            dist.all_gather_into_tensor(yg, yl)
-            backend.interleave_columns(yg, yf, world, m, ns, 4, stream=stream)
-            pin_out.copy_(yf, non_blocking=True)
+            if fused:
+                y = sharded.run_exchange(xd, m, stream=stream, out_dtype=torch.float32)
+            else:
+                sharded.run_device(xd, yf, m, stream=stream)
+                y = yf
+            pin_out.copy_(y, non_blocking=True)
             torch.cuda.synchronize(dev)
         for _ in range(2):
             one()
@@ -490,6 +526,8 @@ def e2e_measure(backend, lin, torch, dist, dev, args, world, m, k, n, ns, x_host
     return {"value": 2.0 * m * k * n / dt / 1e12, "unit": "TOPS", "ms_per_step": dt * 1e3,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "api": "qlinear_run_f32 (host f32 in/out)" if world == 1 else
+                   "H2D f32 -> qlinear_run_device_scatter (fused NVLink output exchange) -> "
+                   "D2H f32" if args.exchange == "fused" else
                    "H2D f32 -> qlinear_run_device -> NCCL all-gather -> "
                    "qlinear_interleave_columns -> D2H f32"}
 

@@ -171,6 +171,35 @@ QLINEAR_API int qlinear_run_device(qlinear_backend *backend, const qlinear_weigh
                        const void *a_dev, int a_type, void *c_dev, int c_type, long long ldc,
                        int rows, unsigned flags, void *stream);
 
+/* Split-N output exchange fused into the kernels (no reference counterpart; one process per
+ * GPU, the layer's output columns sharded over the GPUs of one node): like
+ * qlinear_run_device, but the kernels' epilogues store every output element into each of
+ * the ndev (1..8) buffers c_devs[] -- this GPU's own and the peers' (opened with
+ * qlinear_peer_buffer_open) -- at row m, column col_offset + n, row stride ldc.  The stores
+ * to peers cross NVLink while the kernel computes; the kernels end with a system-scope
+ * fence, so a collective issued on the same stream afterwards (e.g. a one-element NCCL
+ * all-reduce) tells every peer that this rank's columns are in place.  The caller must keep
+ * peers from reading the destination rows until then, and from being written by a later
+ * call while they still read them.  SwiGLU through the tensor-core path (rows > 8) is not
+ * supported here (QLINEAR_ERR_UNSUPPORTED). */
+QLINEAR_API int qlinear_run_device_scatter(qlinear_backend *backend, const qlinear_weights *weights,
+                                           const void *a_dev, int a_type, void *const *c_devs,
+                                           int ndev, int c_type, long long ldc, long long col_offset,
+                                           int rows, unsigned flags, void *stream);
+
+/* Exchange buffers for qlinear_run_device_scatter: qlinear_peer_buffer_create allocates
+ * `bytes` of device memory on the backend's GPU and writes its CUDA IPC handle
+ * (QLINEAR_IPC_HANDLE_BYTES bytes) to ipc_handle; another process opens that handle with
+ * qlinear_peer_buffer_open and gets a pointer its kernels can store to over NVLink;
+ * qlinear_peer_buffer_free releases either kind (opened = 1 for a pointer from
+ * qlinear_peer_buffer_open). */
+#define QLINEAR_IPC_HANDLE_BYTES 64
+QLINEAR_API int qlinear_peer_buffer_create(qlinear_backend *backend, size_t bytes, void **dev_ptr,
+                                           unsigned char *ipc_handle);
+QLINEAR_API int qlinear_peer_buffer_open(qlinear_backend *backend, const unsigned char *ipc_handle,
+                                         void **dev_ptr);
+QLINEAR_API int qlinear_peer_buffer_free(qlinear_backend *backend, void *dev_ptr, int opened);
+
 /* Activation quantisation alone (parity export of the int8 codes): a_dev [rows][K] ->
  * codes_dev int8 [rows][K], scales_dev f32 [rows], rowsums_dev int32 [rows] (may be NULL;
  * sum of the row's codes).  Asynchronous on `stream`. */
@@ -223,6 +252,13 @@ QLINEAR_API int qlinear_run_device_noalloc(const qlinear_weights *weights, const
 /* Reads and clears the backend's device error word (bounded waits that gave up);
  * synchronizes `stream` first.  Returns QLINEAR_OK or QLINEAR_ERR_TIMEOUT. */
 QLINEAR_API int qlinear_backend_check(qlinear_backend *backend, void *stream);
+
+/* Failure-path self-test (no reference counterpart): launches one warp that waits on an
+ * mbarrier nothing arrives on.  After limit_ns (1 ms .. 2 s) the wait gives up, records the
+ * timeout in the backend's device error word and the kernel returns, as a stuck pipeline
+ * stage of the GEMM would.  Returns QLINEAR_ERR_TIMEOUT, the expected result (the error word
+ * is cleared and the backend stays usable); QLINEAR_ERR_PARAM for a limit out of range. */
+QLINEAR_API int qlinear_selftest_wait_timeout(qlinear_backend *backend, unsigned long long limit_ns);
 
 /* Replaces Backend::stats (src/npu.rs:631-661): JSON text into buf (NUL-terminated).
  * Returns the length needed (excluding NUL) or a negative status. */

@@ -37,6 +37,7 @@ class QLinearUnavailable(RuntimeError):
 
 BACKEND_W4_PACKED_ONLY = 1
 BACKEND_GEMM_STREAM_K = 2
+IPC_HANDLE_BYTES = 64
 
 
 class BackendConfig(ctypes.Structure):
@@ -71,6 +72,12 @@ SIGNATURES = {
     "qlinear_run_f32": (_I, [_P, _P, _P, _P, _I]),
     "qlinear_run_swiglu_f32": (_I, [_P, _P, _P, _P, _I]),
     "qlinear_run_f32_ex": (_I, [_P, _P, _P, _P, ctypes.c_longlong, _I, ctypes.c_uint]),
+    "qlinear_selftest_wait_timeout": (_I, [_P, ctypes.c_ulonglong]),
+    "qlinear_run_device_scatter": (_I, [_P, _P, _P, _I, _P, _I, _I, ctypes.c_longlong,
+                                        ctypes.c_longlong, _I, ctypes.c_uint, _P]),
+    "qlinear_peer_buffer_create": (_I, [_P, ctypes.c_size_t, _P, _P]),
+    "qlinear_peer_buffer_open": (_I, [_P, _P, _P]),
+    "qlinear_peer_buffer_free": (_I, [_P, _P, _I]),
     "qlinear_run_device": (_I, [_P, _P, _P, _I, _P, _I, ctypes.c_longlong, _I, ctypes.c_uint, _P]),
     "qlinear_act_quant_device": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _P]),
     "qlinear_run_device_noalloc": (_I, [_P, _P, _I, _P, _I, ctypes.c_longlong, _I, _P]),

@@ -72,13 +72,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 // recording the timeout in *err and in the CTA-wide abort flag) if it gave up, or if
 // another role of the CTA already gave up.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsigned *err,
-                                          volatile int *abort_flag) {
+                                          volatile int *abort_flag,
+                                          unsigned long long limit_ns = QL_WAIT_NS) {
     if (mbar_try_wait(bar, parity)) return true;
     unsigned long long t0 = global_ns();
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (global_ns() - t0 > QL_WAIT_NS) {
+        if (global_ns() - t0 > limit_ns) {
             *abort_flag = 1;
             if (err) atomicOr(err, QL_DEVERR_TIMEOUT);
             return false;

@@ -73,7 +73,8 @@ struct GemmArgs {
     const float *wscale;
     const float *ascale;
     const int32_t *rowsum;
-    void *out;
+    void *out;             // the output, when one buffer takes it (otherwise the OutputSet
+                           // parameter of a SCATTER kernel)
     long long ldc;
     int M, N, nkb;
     int tok, stages, n_tok_tiles, num_tiles;
@@ -192,10 +193,14 @@ __device__ __forceinline__ uint64_t smem_desc_sw128_k(const void *tile) {
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-template <int BITS, typename OutT>
+// SCATTER: the epilogue stores every element to each of outs' destinations (the split-N
+// exchange); without it, to p.out alone and outs is unused.  The destinations are a separate
+// trailing parameter, not a GemmArgs field: growing GemmArgs changed the register allocation
+// of the single-output kernel (168 -> 150 registers) and measured 2.2x slower on B200.
+template <int BITS, typename OutT, bool SCATTER>
 __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap amap,
-                const GemmArgs p) {
+                const GemmArgs p, const OutputSet outs) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                 ~uintptr_t(1023));
@@ -343,7 +348,6 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
         const int sub = (int)rank * EPI_WARPS + (warp - 2);  // this warp's part of a tile
         const int chl = (int)rank * CH_CTA + q * 32 + lane;  // channel within the tile
         uint32_t local = 0;
-        OutT *out = static_cast<OutT *>(p.out);
         // Activation scales (and W4 row sums) of this warp's columns, loaded once per tile:
         // column c of the warp's range sits in lane c % 32 of register c / 32.
         float sa_r[4];
@@ -357,6 +361,7 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                 rs_r[i] = (BITS == 4 && v) ? p.rowsum[m] : 0;
             }
         };
+        OutT *out = static_cast<OutT *>(p.out);
         // dequantise and store chunk cc (columns 16 cc .. 16 cc + 15 of the warp's range)
         auto emit16 = [&](const uint32_t (&r)[16], int cc, int tok_base, int ch, bool chv,
                           float sw) {
@@ -369,11 +374,26 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                 if (chv && m < p.M) {
                     int acc = (int)r[j];
                     if (BITS == 4) acc -= 8 * rs;
-                    if constexpr (std::is_same<OutT, int32_t>::value) {
-                        out[(long long)m * p.ldc + ch] = acc;
+                    if constexpr (!SCATTER) {
+                        if constexpr (std::is_same<OutT, int32_t>::value) {
+                            out[(long long)m * p.ldc + ch] = acc;
+                        } else {
+                            const float y = __fmul_rn(__fmul_rn(__int2float_rn(acc), sa), sw);
+                            out[(long long)m * p.ldc + ch] = OutCvt<OutT>::from(y);
+                        }
                     } else {
-                        const float y = __fmul_rn(__fmul_rn(__int2float_rn(acc), sa), sw);
-                        out[(long long)m * p.ldc + ch] = OutCvt<OutT>::from(y);
+                        OutT v;
+                        if constexpr (std::is_same<OutT, int32_t>::value)
+                            v = acc;
+                        else
+                            v = OutCvt<OutT>::from(
+                                __fmul_rn(__fmul_rn(__int2float_rn(acc), sa), sw));
+                        const long long idx = (long long)m * p.ldc + outs.col0 + ch;
+                        // compile-time indices into the parameter array (a run-time index
+                        // would copy it to local memory)
+#pragma unroll
+                        for (int d = 0; d < kMaxOutputs; d++)
+                            if (d < outs.count) static_cast<OutT *>(outs.dst[d])[idx] = v;
                     }
                 }
             }
@@ -488,6 +508,9 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
             }
             if (lane == 0) p.sk_cnt[slot * (2 * EPI_WARPS) + sub] = 0;
         }
+        // peers' copies of the output: visible system-wide before the next work on this
+        // stream (the collective that tells the peers the output is complete)
+        if constexpr (SCATTER) __threadfence_system();
     } else {
         // ------------------------------------------------------------ W4 converter
         if constexpr (BITS == 4) {
@@ -571,10 +594,11 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
     }
 }
 
-template <int BITS, typename OutT>
-cudaError_t launch_t(const CUtensorMap &wmap, const CUtensorMap &amap, const GemmArgs &args,
-                     const GemmPlan &plan, bool pdl, cudaStream_t stream) {
-    auto kern = gemm_kernel<BITS, OutT>;
+template <int BITS, typename OutT, bool SCATTER>
+cudaError_t launch_s(const CUtensorMap &wmap, const CUtensorMap &amap, const GemmArgs &args,
+                     const OutputSet &outs, const GemmPlan &plan, bool pdl,
+                     cudaStream_t stream) {
+    auto kern = gemm_kernel<BITS, OutT, SCATTER>;
     // The opt-in shared-memory limit is a per-device, per-kernel attribute: set it once per
     // device (an attribute call per launch costs host time).
     static int configured[64] = {0};
@@ -602,7 +626,17 @@ cudaError_t launch_t(const CUtensorMap &wmap, const CUtensorMap &amap, const Gem
     attr[1].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, kern, wmap, amap, args);
+    return cudaLaunchKernelEx(&cfg, kern, wmap, amap, args, outs);
+}
+
+// One destination: p.out (offset by the column offset); several: the SCATTER kernel.
+template <int BITS, typename OutT>
+cudaError_t launch_t(const CUtensorMap &wmap, const CUtensorMap &amap, GemmArgs args,
+                     const OutputSet &outs, const GemmPlan &plan, bool pdl, cudaStream_t stream) {
+    if (outs.count > 1)
+        return launch_s<BITS, OutT, true>(wmap, amap, args, outs, plan, pdl, stream);
+    args.out = static_cast<OutT *>(outs.dst[0]) + outs.col0;
+    return launch_s<BITS, OutT, false>(wmap, amap, args, outs, plan, pdl, stream);
 }
 
 template <int BITS>
@@ -618,7 +652,7 @@ int pair_capacity_t() {
     qa[0].val.clusterDim.z = 1;
     q.attrs = qa;
     q.numAttrs = 1;
-    auto kern = gemm_kernel<BITS, __half>;
+    auto kern = gemm_kernel<BITS, __half, false>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_DYN_SMEM) !=
         cudaSuccess)
         return 0;
@@ -690,16 +724,16 @@ size_t gemm_sk_bytes(const GemmPlan &plan) {
 }
 
 cudaError_t launch_gemm(const WeightView &w, const CUtensorMap &wmap, const ActView &a,
-                        const CUtensorMap &amap, const GemmPlan &plan, int rows, void *out,
-                        int out_type, long long ldc, unsigned *err, void *sk_ws, bool pdl,
-                        cudaStream_t stream) {
+                        const CUtensorMap &amap, const GemmPlan &plan, int rows,
+                        const OutputSet &out, int out_type, long long ldc, unsigned *err,
+                        void *sk_ws, bool pdl, cudaStream_t stream) {
+    if (out.count < 1 || out.count > kMaxOutputs) return cudaErrorInvalidValue;
     GemmArgs args{};
     args.wq = w.w;
     args.Np = w.Np;
     args.wscale = w.scales;
     args.ascale = a.scales;
     args.rowsum = a.rowsums;
-    args.out = out;
     args.ldc = ldc;
     args.M = rows;
     args.N = w.N;
@@ -720,13 +754,13 @@ cudaError_t launch_gemm(const WeightView &w, const CUtensorMap &wmap, const ActV
         args.sk_ws = reinterpret_cast<int32_t *>(static_cast<char *>(sk_ws) + SK_CNT_BYTES);
     }
     if (w.bits == 8) {
-        if (out_type == kF16) return launch_t<8, __half>(wmap, amap, args, plan, pdl, stream);
-        if (out_type == kF32) return launch_t<8, float>(wmap, amap, args, plan, pdl, stream);
-        return launch_t<8, int32_t>(wmap, amap, args, plan, pdl, stream);
+        if (out_type == kF16) return launch_t<8, __half>(wmap, amap, args, out, plan, pdl, stream);
+        if (out_type == kF32) return launch_t<8, float>(wmap, amap, args, out, plan, pdl, stream);
+        return launch_t<8, int32_t>(wmap, amap, args, out, plan, pdl, stream);
     }
-    if (out_type == kF16) return launch_t<4, __half>(wmap, amap, args, plan, pdl, stream);
-    if (out_type == kF32) return launch_t<4, float>(wmap, amap, args, plan, pdl, stream);
-    return launch_t<4, int32_t>(wmap, amap, args, plan, pdl, stream);
+    if (out_type == kF16) return launch_t<4, __half>(wmap, amap, args, out, plan, pdl, stream);
+    if (out_type == kF32) return launch_t<4, float>(wmap, amap, args, out, plan, pdl, stream);
+    return launch_t<4, int32_t>(wmap, amap, args, out, plan, pdl, stream);
 }
 
 }  // namespace ql

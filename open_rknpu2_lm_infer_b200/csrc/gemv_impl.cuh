@@ -1,0 +1,532 @@
+// gemv_impl.cuh -- decode path (rows <= 8): stream the packed weights from HBM once.
+//
+// The kernel and its launch templates, instantiated in two translation units: gemv.cu (one
+// output buffer) and gemv_scatter.cu (the split-N exchange: every output element stored to
+// this GPU's buffer and to the peers').  Two units so the two sets compile in parallel.
+//
+// acc[m][n] = sum_k q[m][k] * w[k][n] exactly in int32 (src/npu.rs:1111-1116), then
+// y = (f32(acc) * s_a[m]) * s_w[n] (src/npu.rs:1117), written as f32 / fp16 / raw i32;
+// with swiglu, out[m][j] = silu(y[m][j]) * y[m][N/2 + j] (src/npu.rs:1202-1208).
+//
+// Work split: CTA c (one per SM, 16 warps) owns the contiguous output rows [r0, r1); warp w
+// owns the CTA's rows w, w + 16, ...  A task is one chunk of one row (with swiglu: the gate
+// row n and its up row N/2 + n together): U 16-byte units per lane, i.e. 512*U contiguous
+// bytes per segment, read with ld.global.nc.L1::no_allocate straight into registers.  A warp
+// keeps D tasks in flight in a register ring (D*U*16 bytes per lane, about 192 KB per SM in
+// all), issuing task t + D as soon as task t's registers are consumed, and it issues its
+// first D tasks before the activation prologue, so the weight stream starts at the first
+// instruction of the kernel.  There is no shared-memory staging and no barrier on the
+// stream path: measured against a bulk-copy ring with producer/consumer mbarriers, this
+// streams the same bytes in about two thirds of the time on B200 (the ring's hand-offs
+// between warps, not HBM, limited it).
+//
+// Products use dp4a (s8 x s8 for W8, u8 x s8 for W4's offset-binary nibbles, corrected by
+// 8*sum(q) in the epilogue); a row's MT sums are reduced across the warp once with a halving
+// butterfly and its outputs written by the lanes that hold them.  The CTA's weight scales are
+// staged in shared memory at the start, so the per-row epilogue touches no global memory
+// but its store.
+//
+// Activations: either codes from the quantisation kernel (int8 [M][Kp] plus scales and row
+// sums) or -- the fused decode path -- the raw fp16 / f32 rows, which the CTA quantises in
+// the prologue while its first tasks are in flight (a8_row_scale / a8_code: the same
+// arithmetic as act_quant.cu, so the codes are identical).
+#pragma once
+#include "common.cuh"
+#include "kernels.h"
+
+#include <algorithm>
+#include <type_traits>
+
+namespace ql {
+
+namespace {
+
+constexpr int kWarps = 16;
+constexpr int kThreads = kWarps * 32;
+constexpr int kSmemBudget = 220 * 1024;
+constexpr int kMaxUnits = 16;        // units per lane per task (longer rows are split in chunks)
+constexpr int kMaxUnitsSwiglu = 8;   // swiglu tasks carry two rows
+
+// Register ring depth for NSEG*U units per lane per task: about 96 data registers per thread
+// with one or two activation rows, less with more (their partial sums need registers too).
+__host__ __device__ constexpr int ring_depth(int units, int mt) {
+    return (mt <= 2 ? 24 : mt == 4 ? 16 : 12) / units < 1 ? 1
+         : (mt <= 2 ? 24 : mt == 4 ? 16 : 12) / units > 8 ? 8
+         : (mt <= 2 ? 24 : mt == 4 ? 16 : 12) / units;
+}
+
+// The per-lane unit counts the kernel is built for.
+__host__ __device__ constexpr int round_units(int u) {
+    return u <= 1 ? 1 : u <= 2 ? 2 : u <= 3 ? 3 : u <= 4 ? 4 : u <= 5 ? 5 : u <= 6 ? 6
+         : u <= 8 ? 8 : u <= 10 ? 10 : u <= 12 ? 12 : 16;
+}
+
+// Reduce V = 2^p values per lane across the warp; afterwards lane l holds the full sum of
+// value index l / (32 / V) in v[0] (V - 1 + 5 - log2 V shuffles instead of 5 per value).
+template <int V>
+__device__ __forceinline__ void warp_reduce_spread(int (&v)[V], int lane) {
+    int off = 16;
+#pragma unroll
+    for (int n = V; n > 1; n >>= 1) {
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int i = 0; i < n / 2; i++) {
+            const int send = upper ? v[i] : v[i + n / 2];
+            const int keep = upper ? v[i + n / 2] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+        off >>= 1;
+    }
+    for (; off >= 1; off >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
+}
+
+__device__ __forceinline__ void store_typed(void *out, int type, long long idx, float y, int raw) {
+    if (type == kF16)
+        static_cast<__half *>(out)[idx] = __float2half_rn(y);
+    else if (type == kF32)
+        static_cast<float *>(out)[idx] = y;
+    else
+        static_cast<int32_t *>(out)[idx] = raw;
+}
+
+// Store one output element into every destination of the set (this GPU's buffer and, for
+// the split-N exchange, the peers').
+__device__ __forceinline__ void store_all(const OutputSet &o, int type, long long idx, float y,
+                                          int raw) {
+#pragma unroll  // compile-time indices into the parameter array (no local-memory copy)
+    for (int d = 0; d < kMaxOutputs; d++)
+        if (d < o.count) store_typed(o.dst[d], type, idx + o.col0, y, raw);
+}
+
+struct GemvArgs {
+    const uint8_t *wq;
+    const float *wscale;
+    int N, Kp, K;
+    const void *xin;
+    int in_type;
+    long long ldx;
+    int round_mode;
+    const float *ascale;
+    const int32_t *rowsum;
+    int M;
+    void *out;  // the output when one buffer takes it; several: the kernel's OutputSet
+    int out_type;
+    long long ldc;
+    int rows_per_cta;  // output rows (channels, or gate rows with swiglu) per CTA
+    int nch;           // chunks per row
+    unsigned *err;
+};
+
+// Quantise the call's rows into xs (codes [MT][Kp], zero beyond M and K) and set s_scale /
+// s_rowsum.  TIn: __half or float; K and ldx are multiples of 16 / sizeof(TIn) and the rows
+// 16-byte aligned (gemv_can_fuse).
+template <int MT, typename TIn>
+__device__ __forceinline__ void quantise_rows(const GemvArgs &p, uint8_t *xs, float *s_scale,
+                                              int *s_rowsum, float (*s_red)[MT],
+                                              int (*s_redi)[MT]) {
+    constexpr int VEC = 16 / sizeof(TIn);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const TIn *x = static_cast<const TIn *>(p.xin);
+    const int nvec = p.K / VEC;
+    auto widen = [](const uint4 &raw, float (&f)[VEC]) {
+        if constexpr (VEC == 8) {
+            const __half2 *h = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float2 t = __half22float2(h[i]);
+                f[2 * i] = t.x;
+                f[2 * i + 1] = t.y;
+            }
+        } else {
+            f[0] = __uint_as_float(raw.x); f[1] = __uint_as_float(raw.y);
+            f[2] = __uint_as_float(raw.z); f[3] = __uint_as_float(raw.w);
+        }
+    };
+    // pass 1: per-row max |x| (fmaxf ignores NaN, like Rust's f32::max)
+    float am[MT];
+#pragma unroll
+    for (int m = 0; m < MT; m++) am[m] = 0.0f;
+    for (int v = tid; v < nvec; v += kThreads) {
+#pragma unroll
+        for (int m = 0; m < MT; m++) {
+            if (m < p.M) {
+                float f[VEC];
+                widen(__ldg(reinterpret_cast<const uint4 *>(x + (long long)m * p.ldx) + v), f);
+#pragma unroll
+                for (int e = 0; e < VEC; e++) am[m] = fmaxf(am[m], fabsf(f[e]));
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < MT; m++) {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) am[m] = fmaxf(am[m], __shfl_xor_sync(0xffffffffu, am[m], o));
+        if (lane == 0) s_red[warp][m] = am[m];
+    }
+    __syncthreads();
+    __shared__ float s_inv[MT];
+    if (tid < MT) {
+        float a = 0.0f;
+        for (int w = 0; w < kWarps; w++) a = fmaxf(a, s_red[w][tid]);
+        float sc, inv;
+        a8_row_scale(a, sc, inv);
+        s_scale[tid] = sc;
+        s_inv[tid] = inv;
+    }
+    __syncthreads();
+    float inv[MT];
+#pragma unroll
+    for (int m = 0; m < MT; m++) inv[m] = s_inv[m];
+    // pass 2: codes (rows >= M and the K padding are zero)
+    int sum[MT];
+#pragma unroll
+    for (int m = 0; m < MT; m++) sum[m] = 0;
+    for (int v = tid; v < nvec; v += kThreads) {
+#pragma unroll
+        for (int m = 0; m < MT; m++) {
+            uint32_t w[VEC / 4];
+#pragma unroll
+            for (int g = 0; g < VEC / 4; g++) w[g] = 0;
+            if (m < p.M) {
+                float f[VEC];
+                widen(__ldg(reinterpret_cast<const uint4 *>(x + (long long)m * p.ldx) + v), f);
+#pragma unroll
+                for (int g = 0; g < VEC / 4; g++) {
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const int q = a8_code(f[4 * g + e], inv[m], p.round_mode);
+                        sum[m] += q;
+                        w[g] |= (uint32_t)(q & 0xff) << (8 * e);
+                    }
+                }
+            }
+            if constexpr (VEC == 8)
+                *reinterpret_cast<uint2 *>(xs + m * p.Kp + v * 8) = make_uint2(w[0], w[1]);
+            else
+                *reinterpret_cast<uint32_t *>(xs + m * p.Kp + v * 4) = w[0];
+        }
+    }
+    for (int i = p.K + tid; i < p.Kp; i += kThreads) {
+#pragma unroll
+        for (int m = 0; m < MT; m++) xs[m * p.Kp + i] = 0;
+    }
+#pragma unroll
+    for (int m = 0; m < MT; m++) {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) sum[m] += __shfl_xor_sync(0xffffffffu, sum[m], o);
+        if (lane == 0) s_redi[warp][m] = sum[m];
+    }
+    __syncthreads();
+    if (tid < MT) {
+        int t = 0;
+        for (int w = 0; w < kWarps; w++) t += s_redi[w][tid];
+        s_rowsum[tid] = t;
+    }
+}
+
+// The scatter kernel's destinations; the single-output kernel takes an empty parameter in
+// their place and stores to p.out alone.  (Measured on B200: a run-time choice between the
+// two in one kernel cost the M=1 decode call 0.4 us of its 9 us.)
+struct NoOutputs {};
+template <bool SCATTER> struct OutsParam { using type = NoOutputs; };
+template <> struct OutsParam<true> { using type = OutputSet; };
+
+// BITS: 4/8.  MT: activation rows held (>= M).  U: 16-byte units per lane per task segment.
+// SCATTER: store every output element to each of outs' destinations.
+template <int BITS, int MT, bool SWIGLU, int U, bool SCATTER>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemv_kernel(const GemvArgs p, const typename OutsParam<SCATTER>::type outs) {
+    constexpr int NSEG = SWIGLU ? 2 : 1;
+    constexpr int D = ring_depth(NSEG * U, MT);
+    constexpr int V = MT;  // sums a warp reduces per row and segment
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ float s_scale[MT];
+    __shared__ int s_rowsum[MT];
+    __shared__ float s_red[kWarps][MT];
+    __shared__ int s_redi[kWarps][MT];
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int row_bytes = BITS == 8 ? p.Kp : p.Kp / 2;
+    const int upr = row_bytes / 16;  // 16-byte units per row
+    const int nrows_out = SWIGLU ? p.N / 2 : p.N;
+    const int r0 = blockIdx.x * p.rows_per_cta;
+    const int nr = max(0, min(nrows_out, r0 + p.rows_per_cta) - r0);
+    const int my_rows = nr > warp ? (nr - warp + kWarps - 1) / kWarps : 0;
+    const int ntask = my_rows * p.nch;
+    const uint8_t *seg0 = p.wq + (long long)r0 * row_bytes;                 // gate / only rows
+    const uint8_t *seg1 = p.wq + ((long long)p.N / 2 + r0) * row_bytes;     // up rows (swiglu)
+
+    uint8_t *xs = smem;                                         // [MT][Kp] codes
+    float *ws = reinterpret_cast<float *>(xs + (size_t)MT * p.Kp);  // [NSEG][rows_per_cta]
+
+    // Task t of this warp: local row warp + (t / nch) * kWarps, chunk t % nch.
+    uint4 ring[D][NSEG * U];
+    auto issue = [&](int t, uint4 (&dst)[NSEG * U]) {
+        const int i = t / p.nch, c = t - i * p.nch;
+        const long long off = (long long)(warp + i * kWarps) * row_bytes;
+        const int j0 = c * 32 * U + lane;
+#pragma unroll
+        for (int s = 0; s < NSEG; s++) {
+            const uint8_t *row = (s == 0 ? seg0 : seg1) + off;
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int j = j0 + u * 32;
+                dst[s * U + u] = j < upr ? ldg_stream(row + j * 16) : make_uint4(0, 0, 0, 0);
+            }
+        }
+    };
+#pragma unroll
+    for (int d = 0; d < D; d++)
+        if (d < ntask) issue(d, ring[d]);
+
+    // Scales of the CTA's rows (plain loads, consumed after the prologue's barriers).
+    for (int i = tid; i < nr; i += kThreads) {
+        ws[i] = p.wscale[r0 + i];
+        if (SWIGLU) ws[p.rows_per_cta + i] = p.wscale[p.N / 2 + r0 + i];
+    }
+
+    // ---------------------------------------------------------------- activation codes
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (p.in_type == kF16) {
+        quantise_rows<MT, __half>(p, xs, s_scale, s_rowsum, s_red, s_redi);
+    } else if (p.in_type == kF32) {
+        quantise_rows<MT, float>(p, xs, s_scale, s_rowsum, s_red, s_redi);
+    } else {
+        const int8_t *codes = static_cast<const int8_t *>(p.xin);
+        const int n16 = MT * p.Kp / 16;
+        for (int i = tid; i < n16; i += kThreads) {
+            const int m = (i * 16) / p.Kp;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (m < p.M) v = *reinterpret_cast<const uint4 *>(codes + (long long)i * 16);
+            reinterpret_cast<uint4 *>(xs)[i] = v;
+        }
+        if (tid < MT) {
+            s_scale[tid] = tid < p.M ? p.ascale[tid] : 0.0f;
+            s_rowsum[tid] = tid < p.M ? p.rowsum[tid] : 0;
+        }
+    }
+    __syncthreads();
+
+    // ---------------------------------------------------------------- stream the weights
+    int acc[NSEG][V];
+#pragma unroll
+    for (int s = 0; s < NSEG; s++)
+#pragma unroll
+        for (int m = 0; m < V; m++) acc[s][m] = 0;
+    for (int t0 = 0; t0 < ntask; t0 += D) {
+#pragma unroll
+        for (int d = 0; d < D; d++) {
+            const int t = t0 + d;
+            if (t >= ntask) break;
+            const int i = t / p.nch, c = t - i * p.nch;
+            const int j0 = c * 32 * U + lane;
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int j = j0 + u * 32;
+                if (j < upr) {
+#pragma unroll
+                    for (int s = 0; s < NSEG; s++) {
+                        const uint4 wv = ring[d][s * U + u];
+                        if constexpr (BITS == 8) {
+#pragma unroll
+                            for (int m = 0; m < MT; m++) {
+                                const uint4 xv = *reinterpret_cast<const uint4 *>(xs + m * p.Kp + j * 16);
+                                int a = dp4a_ss(wv.x, xv.x, acc[s][m]);
+                                a = dp4a_ss(wv.y, xv.y, a);
+                                a = dp4a_ss(wv.z, xv.z, a);
+                                acc[s][m] = dp4a_ss(wv.w, xv.w, a);
+                            }
+                        } else {
+                            // 16 packed bytes = 32 codes k = 32j .. 32j+31; word q covers 8
+                            // codes: low nibbles k 8q..8q+3, high nibbles k 8q+4..8q+7.
+                            const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                            for (int m = 0; m < MT; m++) {
+                                const uint4 xa = *reinterpret_cast<const uint4 *>(xs + m * p.Kp + j * 32);
+                                const uint4 xb =
+                                    *reinterpret_cast<const uint4 *>(xs + m * p.Kp + j * 32 + 16);
+                                const uint32_t x8[8] = {xa.x, xa.y, xa.z, xa.w,
+                                                        xb.x, xb.y, xb.z, xb.w};
+                                int a = acc[s][m];
+#pragma unroll
+                                for (int q = 0; q < 4; q++) {
+                                    a = dp4a_us(w4[q] & 0x0F0F0F0Fu, x8[2 * q], a);
+                                    a = dp4a_us((w4[q] >> 4) & 0x0F0F0F0Fu, x8[2 * q + 1], a);
+                                }
+                                acc[s][m] = a;
+                            }
+                        }
+                    }
+                }
+            }
+            if (t + D < ntask) issue(t + D, ring[d]);  // refill the slot just consumed
+            if (c != p.nch - 1) continue;              // the row has more chunks
+
+            // ---------------------------------------------------------- row epilogue
+            const int lr = warp + i * kWarps;
+            int tot[NSEG];
+#pragma unroll
+            for (int s = 0; s < NSEG; s++) {
+                warp_reduce_spread<V>(acc[s], lane);
+                tot[s] = acc[s][0];
+#pragma unroll
+                for (int m = 0; m < V; m++) acc[s][m] = 0;
+            }
+            const int m = lane / (32 / V);  // activation row whose totals this lane holds
+            if ((lane % (32 / V)) == 0 && m < p.M) {
+                if (BITS == 4) {
+#pragma unroll
+                    for (int s = 0; s < NSEG; s++) tot[s] -= 8 * s_rowsum[m];
+                }
+                const int n = r0 + lr;
+                const float sa = s_scale[m];
+                if constexpr (SWIGLU) {
+                    const float g = __fmul_rn(__fmul_rn(__int2float_rn(tot[0]), sa), ws[lr]);
+                    const float up = __fmul_rn(__fmul_rn(__int2float_rn(tot[NSEG - 1]), sa),
+                                               ws[p.rows_per_cta + lr]);
+                    const float y = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), up);
+                    if constexpr (SCATTER)
+                        store_all(outs, p.out_type, (long long)m * p.ldc + n, y, 0);
+                    else
+                        store_typed(p.out, p.out_type, (long long)m * p.ldc + n, y, 0);
+                } else {
+                    const float y = __fmul_rn(__fmul_rn(__int2float_rn(tot[0]), sa), ws[lr]);
+                    if constexpr (SCATTER)
+                        store_all(outs, p.out_type, (long long)m * p.ldc + n, y, tot[0]);
+                    else
+                        store_typed(p.out, p.out_type, (long long)m * p.ldc + n, y, tot[0]);
+                }
+            }
+        }
+    }
+    // peers' copies of the output: visible system-wide before the next work on this stream
+    if constexpr (SCATTER) __threadfence_system();
+}
+
+inline int mt_of(int rows) { return rows <= 1 ? 1 : rows <= 2 ? 2 : rows <= 4 ? 4 : 8; }
+
+struct Plan {
+    int rows_per_cta, grid, nch, units;
+    size_t smem;
+};
+
+// Rows per CTA (one CTA per SM), chunks per row and units per lane, shared memory.
+inline bool plan(int rows, int Kp, int N, int bits, bool swiglu, int num_sms, Plan *pl) {
+    if (rows < 1 || rows > 8 || num_sms < 1) return false;
+    const int nrows = swiglu ? N / 2 : N;
+    if (nrows < 1) return false;
+    const int per = (nrows + num_sms - 1) / num_sms;
+    const int upr = (bits == 8 ? Kp : Kp / 2) / 16;
+    const int lane_units = (upr + 31) / 32;
+    const int maxu = swiglu ? kMaxUnitsSwiglu : kMaxUnits;
+    const int nch = (lane_units + maxu - 1) / maxu;
+    const size_t smem = (size_t)mt_of(rows) * Kp + (size_t)(swiglu ? 2 : 1) * per * 4;
+    if (smem > (size_t)kSmemBudget) return false;
+    pl->rows_per_cta = per;
+    pl->grid = (nrows + per - 1) / per;
+    pl->nch = nch;
+    pl->units = round_units((lane_units + nch - 1) / nch);
+    pl->smem = smem;
+    return true;
+}
+
+template <int BITS, int MT, bool SWIGLU, int U, bool SCATTER>
+cudaError_t launch_t(const WeightView &w, const GemvInput &in, int rows, const OutputSet &out, int out_type,
+                     long long ldc, const Plan &pl, cudaStream_t stream) {
+    GemvArgs a{};
+    a.wq = w.w;
+    a.wscale = w.scales;
+    a.N = w.N;
+    a.Kp = w.Kp;
+    a.K = w.K;
+    a.xin = in.x;
+    a.in_type = in.type;
+    a.ldx = in.ldx;
+    a.round_mode = in.round_mode;
+    a.ascale = in.ascale;
+    a.rowsum = in.rowsum;
+    a.M = rows;
+    // one destination: offset by the column offset here; scatter: the kernel adds it
+    a.out = SCATTER ? nullptr
+                    : static_cast<char *>(out.dst[0]) + out.col0 * (out_type == kF16 ? 2 : 4);
+    a.out_type = out_type;
+    a.ldc = ldc;
+    a.rows_per_cta = pl.rows_per_cta;
+    a.nch = pl.nch;
+    a.err = in.err;
+    auto kern = gemv_kernel<BITS, MT, SWIGLU, U, SCATTER>;
+    static int configured[64] = {0};  // per device: raise the opt-in limit once
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kSmemBudget);
+        if (e != cudaSuccess) return e;
+        configured[dev] = 1;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(pl.grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = pl.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if constexpr (SCATTER)
+        return cudaLaunchKernelEx(&cfg, kern, a, out);
+    else
+        return cudaLaunchKernelEx(&cfg, kern, a, NoOutputs{});
+}
+
+template <int BITS, int MT, bool SWIGLU, bool SCATTER>
+cudaError_t launch_u(const WeightView &w, const GemvInput &in, int rows, const OutputSet &out, int out_type,
+                     long long ldc, const Plan &pl, cudaStream_t stream) {
+#define QL_GEMV_U(u)                                                                      \
+    case u:                                                                               \
+        if constexpr (!SWIGLU || u <= kMaxUnitsSwiglu)                                    \
+            return launch_t<BITS, MT, SWIGLU, u, SCATTER>(w, in, rows, out, out_type, ldc, pl, \
+                                                             stream);                    \
+        return cudaErrorInvalidValue;
+    switch (pl.units) {
+        QL_GEMV_U(1) QL_GEMV_U(2) QL_GEMV_U(3) QL_GEMV_U(4) QL_GEMV_U(5)
+        QL_GEMV_U(6) QL_GEMV_U(8) QL_GEMV_U(10) QL_GEMV_U(12) QL_GEMV_U(16)
+    default: return cudaErrorInvalidValue;
+    }
+#undef QL_GEMV_U
+}
+
+template <int BITS, bool SWIGLU, bool SCATTER>
+cudaError_t launch_mt(const WeightView &w, const GemvInput &in, int rows, const OutputSet &out, int out_type,
+                      long long ldc, const Plan &pl, cudaStream_t stream) {
+    switch (mt_of(rows)) {
+    case 1: return launch_u<BITS, 1, SWIGLU, SCATTER>(w, in, rows, out, out_type, ldc, pl, stream);
+    case 2: return launch_u<BITS, 2, SWIGLU, SCATTER>(w, in, rows, out, out_type, ldc, pl, stream);
+    case 4: return launch_u<BITS, 4, SWIGLU, SCATTER>(w, in, rows, out, out_type, ldc, pl, stream);
+    default: return launch_u<BITS, 8, SWIGLU, SCATTER>(w, in, rows, out, out_type, ldc, pl, stream);
+    }
+}
+
+// Checks the request and launches the kernel built for it.
+template <bool SCATTER>
+cudaError_t launch_checked(const WeightView &w, const GemvInput &in, int rows, const OutputSet &out,
+                           int out_type, long long ldc, bool swiglu, int num_sms,
+                           cudaStream_t stream) {
+    Plan pl;
+    if (!plan(rows, w.Kp, w.N, w.bits, swiglu, num_sms, &pl)) return cudaErrorInvalidValue;
+    if (in.type != kI8Codes && !gemv_can_fuse(in.x, in.type, in.ldx, w.K)) return cudaErrorInvalidValue;
+    if (out_type != kF16 && out_type != kF32 && (out_type != kI32 || swiglu))
+        return cudaErrorInvalidValue;
+    if (out.count < 1 || out.count > kMaxOutputs) return cudaErrorInvalidValue;
+    if (w.bits == 8)
+        return swiglu ? launch_mt<8, true, SCATTER>(w, in, rows, out, out_type, ldc, pl, stream)
+                      : launch_mt<8, false, SCATTER>(w, in, rows, out, out_type, ldc, pl, stream);
+    return swiglu ? launch_mt<4, true, SCATTER>(w, in, rows, out, out_type, ldc, pl, stream)
+                  : launch_mt<4, false, SCATTER>(w, in, rows, out, out_type, ldc, pl, stream);
+}
+
+}  // namespace
+
+}  // namespace ql

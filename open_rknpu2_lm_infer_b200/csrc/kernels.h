@@ -19,6 +19,23 @@ struct WeightView {
     const float *scales;   // device, [Np], zero padded
 };
 
+// Where a kernel writes its output: dst[0] (this GPU's buffer) and, for the split-N
+// exchange, up to kMaxOutputs - 1 peers' buffers mapped into this process (CUDA IPC); the
+// element (m, n) goes to column col0 + n of row m (row stride ldc) of every destination.
+constexpr int kMaxOutputs = 8;
+struct OutputSet {
+    void *dst[kMaxOutputs];
+    int count;
+    long long col0;
+};
+inline OutputSet single_output(void *p) {
+    OutputSet o{};
+    o.dst[0] = p;
+    o.count = 1;
+    o.col0 = 0;
+    return o;
+}
+
 // Activation workspace: codes int8 [rows_cap][Kp], scales f32 [rows_cap], rowsums i32.
 struct ActView {
     const int8_t *codes;
@@ -58,8 +75,12 @@ struct GemvInput {
 // rows <= 8 and the activation codes and the CTA's weight scales fit the GEMV's shared memory
 bool gemv_fits(int rows, int Kp, int N, int bits, bool swiglu, int num_sms);
 bool gemv_can_fuse(const void *x, int type, long long ldx, int K);
-cudaError_t launch_gemv(const WeightView &w, const GemvInput &in, int rows, void *out,
+cudaError_t launch_gemv(const WeightView &w, const GemvInput &in, int rows, const OutputSet &out,
                         int out_type, long long ldc, bool swiglu, int num_sms, cudaStream_t stream);
+// The same with out.count > 1 (launch_gemv forwards to it): the split-N exchange's GEMV.
+cudaError_t launch_gemv_scatter(const WeightView &w, const GemvInput &in, int rows,
+                                const OutputSet &out, int out_type, long long ldc, bool swiglu,
+                                int num_sms, cudaStream_t stream);
 
 // tcgen05 GEMM (any rows).  wmap / amap are the TMA descriptors of the weights and the
 // activation codes (see encode_* below).  out [rows][ldc] of out_type.
@@ -86,9 +107,14 @@ size_t gemm_sk_bytes(const GemmPlan &plan);
 // griddepcontrol.wait before reading the activation codes / scales).  sk_ws: the zeroed
 // stream-K workspace of gemm_sk_bytes(plan) bytes (ignored without stream-K).
 cudaError_t launch_gemm(const WeightView &w, const CUtensorMap &wmap, const ActView &a,
-                        const CUtensorMap &amap, const GemmPlan &plan, int rows, void *out,
+                        const CUtensorMap &amap, const GemmPlan &plan, int rows,
+                        const OutputSet &out,
                         int out_type, long long ldc, unsigned *err, void *sk_ws, bool pdl,
                         cudaStream_t stream);
+
+// Failure-path self-test: one warp waits limit_ns on an mbarrier nobody arrives on, then
+// records QL_DEVERR_TIMEOUT in *err and returns.
+cudaError_t launch_wait_selftest(unsigned *err, unsigned long long limit_ns, cudaStream_t stream);
 
 // SwiGLU over an f32 [rows][N] buffer: out[m][j] = silu(y[m][j]) * y[m][N/2 + j].
 cudaError_t launch_swiglu(const float *y, int rows, int N, void *out, int out_type,

@@ -77,7 +77,7 @@ extern "C" int qlinear_run_device_noalloc(const qlinear_weights *weights, const 
             status = QLINEAR_ERR_CUDA;
         else {
             GemvInput in{codes, kI8Codes, v.Kp, round_mode, scales, rowsums, nullptr};
-            if (launch_gemv(v, in, rows, c_dev, c_type, ldc, false, num_sms, s) != cudaSuccess)
+            if (launch_gemv(v, in, rows, single_output(c_dev), c_type, ldc, false, num_sms, s) != cudaSuccess)
                 status = QLINEAR_ERR_CUDA;
         }
     }

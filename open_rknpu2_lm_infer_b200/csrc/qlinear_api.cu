@@ -271,13 +271,19 @@ int next_prof_events(qlinear_backend *b, const std::array<cudaEvent_t, 3> **out)
     return QLINEAR_OK;
 }
 
+// outs: where the output goes (this GPU's buffer, plus peers' for the split-N exchange);
+// c_dev = outs.dst[0].
 int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_dev, int a_type,
-                    void *c_dev, int c_type, long long ldc, int rows, unsigned flags,
+                    const OutputSet &outs, int c_type, long long ldc, int rows, unsigned flags,
                     cudaStream_t stream) {
     const WeightView &v = w->view;
     const bool swiglu = (flags & QLINEAR_RUN_SWIGLU) != 0;
     const int width = swiglu ? v.N / 2 : v.N;
-    if (rows < 1 || !a_dev || !c_dev || !valid_io_type(a_type)) return QLINEAR_ERR_PARAM;
+    void *c_dev = outs.dst[0];
+    if (rows < 1 || !a_dev || !valid_io_type(a_type) || outs.count < 1 || outs.count > kMaxOutputs)
+        return QLINEAR_ERR_PARAM;
+    for (int d = 0; d < outs.count; d++)
+        if (!outs.dst[d]) return QLINEAR_ERR_PARAM;
     if (c_type != QLINEAR_F32 && c_type != QLINEAR_F16 && c_type != QLINEAR_I32)
         return QLINEAR_ERR_PARAM;
     if (swiglu && (v.N % 2 != 0 || c_type == QLINEAR_I32)) return QLINEAR_ERR_PARAM;
@@ -294,7 +300,7 @@ int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_
             QL_TRY(cudaEventRecord((*ev)[1], stream));
         }
         GemvInput in{a_dev, a_type, v.K, b->round_mode, nullptr, nullptr, b->d_err};
-        const cudaError_t e = launch_gemv(v, in, rows, c_dev, c_type, ldc, swiglu, b->num_sms, stream);
+        const cudaError_t e = launch_gemv(v, in, rows, outs, c_type, ldc, swiglu, b->num_sms, stream);
         if (ev) cudaEventRecord((*ev)[2], stream);
         QL_TRY(e);
         b->launches++;
@@ -322,7 +328,7 @@ int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_
 
     if (gemv_fits(rows, v.Kp, v.N, v.bits, swiglu, b->num_sms)) {
         GemvInput in{codes, kI8Codes, v.Kp, b->round_mode, b->d_ascale, b->d_rowsum, b->d_err};
-        QL_TRY(launch_gemv(v, in, rows, c_dev, c_type, ldc, swiglu, b->num_sms, stream));
+        QL_TRY(launch_gemv(v, in, rows, outs, c_type, ldc, swiglu, b->num_sms, stream));
         b->launches++;
         b->gemv_calls++;
         return QLINEAR_OK;
@@ -344,15 +350,16 @@ int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_
     st = get_amap(b, v.Kp, plan.tok, &amap);
     if (st) return st;
     if (!swiglu) {
-        QL_TRY(launch_gemm(gv, gmap, av, *amap, plan, rows, c_dev, c_type, ldc, b->d_err, b->d_sk,
+        QL_TRY(launch_gemm(gv, gmap, av, *amap, plan, rows, outs, c_type, ldc, b->d_err, b->d_sk,
                            true, stream));
         b->launches++;
     } else {
         st = ensure_dev(reinterpret_cast<void **>(&b->d_y), &b->y_elems,
                         (size_t)rows * v.N * sizeof(float));
         if (st) return st;
-        QL_TRY(launch_gemm(gv, gmap, av, *amap, plan, rows, b->d_y, kF32, v.N, b->d_err, b->d_sk,
-                           true, stream));
+        if (outs.count != 1) return QLINEAR_ERR_UNSUPPORTED;  // the SwiGLU pass writes one buffer
+        QL_TRY(launch_gemm(gv, gmap, av, *amap, plan, rows, single_output(b->d_y), kF32, v.N,
+                           b->d_err, b->d_sk, true, stream));
         QL_TRY(launch_swiglu(b->d_y, rows, v.N, c_dev, c_type, ldc, stream));
         b->launches += 2;
     }
@@ -588,8 +595,61 @@ int qlinear_run_device(qlinear_backend *b, const qlinear_weights *w, const void 
                        void *stream) {
     if (!b || !w || w->backend != b) return QLINEAR_ERR_PARAM;
     DeviceGuard guard(b->device);
-    return run_device_impl(b, w, a_dev, a_type, c_dev, c_type, ldc, rows, flags,
+    return run_device_impl(b, w, a_dev, a_type, single_output(c_dev), c_type, ldc, rows, flags,
                            static_cast<cudaStream_t>(stream));
+}
+
+int qlinear_run_device_scatter(qlinear_backend *b, const qlinear_weights *w, const void *a_dev,
+                               int a_type, void *const *c_devs, int ndev, int c_type,
+                               long long ldc, long long col_offset, int rows, unsigned flags,
+                               void *stream) {
+    if (!b || !w || w->backend != b || !c_devs || ndev < 1 || ndev > kMaxOutputs || col_offset < 0)
+        return QLINEAR_ERR_PARAM;
+    const int width = (flags & QLINEAR_RUN_SWIGLU) ? w->view.N / 2 : w->view.N;
+    if (ldc < col_offset + width) return QLINEAR_ERR_PARAM;
+    OutputSet o{};
+    for (int d = 0; d < ndev; d++) o.dst[d] = c_devs[d];
+    o.count = ndev;
+    o.col0 = col_offset;
+    DeviceGuard guard(b->device);
+    return run_device_impl(b, w, a_dev, a_type, o, c_type, ldc, rows, flags,
+                           static_cast<cudaStream_t>(stream));
+}
+
+int qlinear_peer_buffer_create(qlinear_backend *b, size_t bytes, void **dev_ptr,
+                               unsigned char *ipc_handle) {
+    if (!b || !dev_ptr || !ipc_handle || bytes == 0) return QLINEAR_ERR_PARAM;
+    DeviceGuard guard(b->device);
+    void *p = nullptr;
+    QL_TRY(cudaMalloc(&p, bytes));
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return cuda_status(e);
+    }
+    static_assert(sizeof(h) == QLINEAR_IPC_HANDLE_BYTES, "CUDA IPC handle size");
+    std::memcpy(ipc_handle, &h, sizeof(h));
+    *dev_ptr = p;
+    return QLINEAR_OK;
+}
+
+int qlinear_peer_buffer_open(qlinear_backend *b, const unsigned char *ipc_handle, void **dev_ptr) {
+    if (!b || !dev_ptr || !ipc_handle) return QLINEAR_ERR_PARAM;
+    DeviceGuard guard(b->device);
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, ipc_handle, sizeof(h));
+    void *p = nullptr;
+    QL_TRY(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+    *dev_ptr = p;
+    return QLINEAR_OK;
+}
+
+int qlinear_peer_buffer_free(qlinear_backend *b, void *dev_ptr, int opened) {
+    if (!b || !dev_ptr) return QLINEAR_ERR_PARAM;
+    DeviceGuard guard(b->device);
+    QL_TRY(opened ? cudaIpcCloseMemHandle(dev_ptr) : cudaFree(dev_ptr));
+    return QLINEAR_OK;
 }
 
 static int run_host(qlinear_backend *b, const qlinear_weights *w, const float *a_host,
@@ -627,8 +687,8 @@ static int run_host(qlinear_backend *b, const qlinear_weights *w, const float *a
         QL_TRY(cudaMemcpyAsync(d_in + r0 * in_row, h_in + r0 * in_row, n * in_row,
                                cudaMemcpyHostToDevice, b->stream));
     }
-    st = run_device_impl(b, w, b->d_in, QLINEAR_F32, b->d_out, QLINEAR_F32, width, rows, flags,
-                         b->stream);
+    st = run_device_impl(b, w, b->d_in, QLINEAR_F32, single_output(b->d_out), QLINEAR_F32, width,
+                         rows, flags, b->stream);
     if (st) return st;
     // Output: row chunks of ~4 MB, each transfer followed by an event; each chunk is copied
     // to the caller's rows (stride ldc) while the next ones are still in transit.
@@ -745,6 +805,14 @@ int qlinear_backend_check(qlinear_backend *b, void *stream) {
         return QLINEAR_ERR_TIMEOUT;
     }
     return QLINEAR_OK;
+}
+
+int qlinear_selftest_wait_timeout(qlinear_backend *b, unsigned long long limit_ns) {
+    if (!b || limit_ns < 1000000ull || limit_ns > 2000000000ull) return QLINEAR_ERR_PARAM;
+    DeviceGuard guard(b->device);
+    QL_TRY(launch_wait_selftest(b->d_err, limit_ns, b->stream));
+    b->launches++;
+    return qlinear_backend_check(b, b->stream);
 }
 
 int qlinear_backend_stats(const qlinear_backend *b, char *buf, size_t len) {

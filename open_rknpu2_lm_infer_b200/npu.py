@@ -190,6 +190,31 @@ class Backend:
     def check(self, stream=None) -> None:
         _check(self._lib.qlinear_backend_check(self.raw, stream), "device check")
 
+    # -- split-N exchange buffers (qlinear_peer_buffer_*) -----------------------------
+    def peer_buffer_create(self, nbytes: int) -> tuple[int, bytes]:
+        """Device buffer on this backend's GPU + its CUDA IPC handle (for the peers)."""
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * L.IPC_HANDLE_BYTES)()
+        _check(self._lib.qlinear_peer_buffer_create(self.raw, nbytes, ctypes.byref(ptr), handle),
+               "peer buffer create")
+        return int(ptr.value), bytes(handle)
+
+    def peer_buffer_open(self, handle: bytes) -> int:
+        """Map a peer's exchange buffer (its IPC handle) into this process."""
+        ptr = ctypes.c_void_p()
+        h = (ctypes.c_ubyte * L.IPC_HANDLE_BYTES).from_buffer_copy(handle)
+        _check(self._lib.qlinear_peer_buffer_open(self.raw, h, ctypes.byref(ptr)), "peer buffer open")
+        return int(ptr.value)
+
+    def peer_buffer_free(self, ptr: int, opened: bool) -> None:
+        _check(self._lib.qlinear_peer_buffer_free(self.raw, ptr, 1 if opened else 0),
+               "peer buffer free")
+
+    def selftest_wait_timeout(self, limit_s: float = 0.2) -> int:
+        """Run the failure-path self-test (a bounded wait that nothing satisfies); returns the
+        status, QLINEAR_ERR_TIMEOUT when the path works."""
+        return int(self._lib.qlinear_selftest_wait_timeout(self.raw, int(limit_s * 1e9)))
+
     def act_quant_device(self, a, rows: int, k: int, codes, scales, rowsums=None,
                          stream=None) -> None:
         """Activation quantisation alone (device buffers); exports the int8 codes."""
@@ -316,3 +341,17 @@ class Linear:
         _check(self._lib.qlinear_run_device(
             self._backend.raw, self._raw, _ptr(a), a_type, _ptr(out), c_type, ldc, rows,
             L.RUN_SWIGLU if swiglu else 0, stream), f"W{self.bits} device run")
+
+    def run_device_scatter(self, a, outs, out_type: int, ldc: int, col_offset: int, rows: int,
+                           swiglu: bool = False, stream=None) -> None:
+        """qlinear_run_device_scatter: the output columns go to column col_offset of every
+        buffer in `outs` (device addresses: this GPU's and the peers' exchange buffers)."""
+        s = str(getattr(a, "dtype", ""))
+        a_type = L.F16 if "float16" in s else L.F32 if "float32" in s else None
+        if a_type is None:
+            raise TypeError(s)
+        arr = (ctypes.c_void_p * len(outs))(*[int(p) for p in outs])
+        _check(self._lib.qlinear_run_device_scatter(
+            self._backend.raw, self._raw, _ptr(a), a_type, arr, len(outs), out_type, ldc,
+            col_offset, rows, L.RUN_SWIGLU if swiglu else 0, stream),
+               f"W{self.bits} device scatter run")

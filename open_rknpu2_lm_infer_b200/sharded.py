@@ -1,12 +1,20 @@
 """Column-parallel (split-N) quantized linear over the ranks of a torch.distributed group.
 
 Each rank holds output channels ``[r*N/g, (r+1)*N/g)`` of one QuantMatrix
-(``qlinear_weights_create_shard``), runs the full activation rows through its shard, and the
-per-rank fp16/f32 slabs are all-gathered over NCCL (NVLink) and assembled into ``[M][N]``
-by ``qlinear_interleave_columns``.  Activations are replicated; the activation quantisation
-runs on every rank and is deterministic, so every rank holds bit-identical codes and the
-assembled output is bit-identical to a single-GPU run.  The reference is single-device;
-this has no counterpart there.
+(``qlinear_weights_create_shard``) and runs the full activation rows through its shard.
+Activations are replicated; the activation quantisation runs on every rank and is
+deterministic, so every rank holds bit-identical codes and the output is bit-identical to a
+single-GPU run.  Two ways to put the [M][N] output together on every rank:
+
+* ``run_device``: the per-rank fp16/f32 slabs are all-gathered over NCCL (NVLink) and
+  assembled into ``[M][N]`` by ``qlinear_interleave_columns``;
+* ``run_exchange`` (``fused_exchange=True``): the kernels' epilogues store each rank's
+  columns straight into every rank's ``[M][N]`` exchange buffer over NVLink while they
+  compute (``qlinear_run_device_scatter``; the buffers are shared through CUDA IPC,
+  ``qlinear_peer_buffer_*``), and a one-element all-reduce afterwards tells every rank the
+  output is complete.  No gather, no assembly pass.
+
+The reference is single-device; this has no counterpart there.
 """
 from __future__ import annotations
 
@@ -30,10 +38,20 @@ def assemble(gathered: np.ndarray) -> np.ndarray:
     return np.ascontiguousarray(np.transpose(gathered, (1, 0, 2)).reshape(m, g * ns))
 
 
+class _DeviceArray:
+    """Zero-copy view of library-owned device memory for torch.as_tensor."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 3,
+                                         "strides": None}
+
+
 class ShardedLinear:
     """One rank's shard of a column-parallel quantized linear."""
 
-    def __init__(self, backend, matrix, group=None):
+    def __init__(self, backend, matrix, group=None, fused_exchange: bool = False,
+                 max_rows: int = 0, out_dtype=None):
         import torch.distributed as dist
         self.backend = backend
         self.group = group
@@ -42,9 +60,75 @@ class ShardedLinear:
         self.n = matrix.n
         self.k = matrix.k
         lo, hi = shard_bounds(matrix.n, self.world, self.rank)
+        self.lo = lo
         self.ns = hi - lo
         self.linear = backend.load_shard(matrix, lo, hi)
         self._bufs = {}
+        self._xbufs = {}  # output dtype -> (own ptr, peer ptrs, [max_rows][N] view, type code)
+        self._default_dtype = None
+        self._flag = None
+        if fused_exchange:
+            self.add_exchange(max_rows, out_dtype)
+
+    def add_exchange(self, max_rows: int, out_dtype=None) -> None:
+        """Collective (every rank, same order): this rank allocates a [max_rows][N] exchange
+        buffer of out_dtype (fp16 default, or f32), shares its CUDA IPC handle and maps the
+        peers' buffers."""
+        import torch
+        import torch.distributed as dist
+        from . import _lib as L
+        if max_rows < 1:
+            raise ValueError("fused exchange needs max_rows >= 1")
+        dtype = out_dtype or torch.float16
+        if dtype not in (torch.float16, torch.float32):
+            raise TypeError(dtype)
+        if dtype in self._xbufs:
+            raise ValueError(f"exchange buffer for {dtype} exists")
+        elem, typestr = (2, "<f2") if dtype == torch.float16 else (4, "<f4")
+        ptr, handle = self.backend.peer_buffer_create(max_rows * self.n * elem)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=self.group)
+        peers = [self.backend.peer_buffer_open(h) for r, h in enumerate(handles) if r != self.rank]
+        dev = torch.device("cuda", self.backend.device)
+        view = torch.as_tensor(_DeviceArray(ptr, (max_rows, self.n), typestr), device=dev)
+        self._xbufs[dtype] = (ptr, peers, view, L.F16 if dtype == torch.float16 else L.F32)
+        if self._default_dtype is None:
+            self._default_dtype = dtype
+        if self._flag is None:
+            self._flag = torch.zeros(1, dtype=torch.float32, device=dev)
+
+    @property
+    def output(self):
+        return self._xbufs[self._default_dtype][2] if self._xbufs else None
+
+    def run_exchange(self, a, rows: int, stream=None, out_dtype=None):
+        """Fused split-N: this rank's columns go straight into every rank's exchange buffer of
+        out_dtype; returns the [rows][N] output (this rank's buffer), complete on every rank
+        once the call's collective is done on the stream.  The caller keeps every rank from
+        reading the previous output while a new call writes it."""
+        import torch.distributed as dist
+        key = out_dtype or self._default_dtype
+        if key not in self._xbufs:
+            raise RuntimeError("no exchange buffer for this output type (add_exchange)")
+        own, peers, view, out_type = self._xbufs[key]
+        if not 1 <= rows <= view.shape[0]:
+            raise ValueError("rows out of range for the exchange buffer")
+        self.linear.run_device_scatter(a, [own] + peers, out_type, self.n, self.lo, rows,
+                                       stream=stream)
+        dist.all_reduce(self._flag, group=self.group)
+        return view[:rows]
+
+    def close(self) -> None:
+        import torch.distributed as dist
+        if self._xbufs:
+            for own, peers, _, _ in self._xbufs.values():
+                for p in peers:
+                    self.backend.peer_buffer_free(p, True)
+            dist.barrier(group=self.group)  # every peer unmapped this rank's buffers
+            for own, _, _, _ in self._xbufs.values():
+                self.backend.peer_buffer_free(own, False)
+            self._xbufs = {}
+        self.linear.close()
 
     def _buf(self, key, shape, dtype, device):
         import torch

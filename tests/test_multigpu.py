@@ -1,5 +1,7 @@
-"""Split-N on 2+ GPUs (NCCL): the assembled output equals the single-GPU output bitwise.
-Runs as torchrun child processes; skipped when fewer than 2 GPUs are visible."""
+"""Split-N on 2+ GPUs: the output assembled after an NCCL all-gather, and the output the
+kernels' epilogues store straight into every rank's exchange buffer (fused exchange over
+NVLink peer memory), both equal the single-GPU output bitwise.  Runs as torchrun child
+processes; skipped when fewer than 2 GPUs are visible."""
 import os
 import subprocess
 import sys
@@ -34,6 +36,17 @@ for bits, k, n, rows in [(4, 2560, 4096, 300), (8, 4096, 2048, 3), (4, 8192, 286
     full.run_device(x, want, rows)
     torch.cuda.synchronize()
     assert torch.equal(out, want), (rank, bits, k, n, rows)
+    # fused exchange: the epilogues store every rank's columns into every rank's buffer
+    for dtype in (torch.float16, torch.float32):
+        fx = ShardedLinear(b, qm, fused_exchange=True, max_rows=rows, out_dtype=dtype)
+        want_t = want if dtype == torch.float16 else torch.empty((rows, n), dtype=dtype, device="cuda")
+        if dtype != torch.float16:
+            full.run_device(x, want_t, rows)
+        for _ in range(2):
+            got = fx.run_exchange(x, rows)
+            torch.cuda.synchronize()
+            assert torch.equal(got, want_t), (rank, "fused", dtype, bits, k, n, rows)
+        fx.close()
     sh.linear.close(); full.close()
 b.check()
 dist.barrier()
