@@ -2,13 +2,15 @@
 """Benchmark of the quantized-linear hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cfg4|cfg0|cfg1|cfg2|...]
+                    [--workload cfg4|cfg0|cfg1|cfg4_m8192] [--exchange fused|gather]
 
 Headline workload (default ``cfg4``): the W4A8 linear K=8192, N=28672 at M=512 tokens,
-split column-parallel over N GPUs (each rank owns N/g output channels), followed by an
-NCCL all-gather of the fp16 outputs and the [g][M][N/g] -> [M][N] assembly.  A step is
-one pass of the path over one batch: act-quant -> tcgen05 GEMM -> (all-gather ->
-assembly).  ``value`` is whole-job TOPS (2*M*K*N / step time, device-timed with CUDA
+split column-parallel over N GPUs (each rank owns N/g output channels); every rank ends
+with the whole fp16 [M][N] output.  With ``--exchange fused`` (default) the GEMM's
+epilogues store each rank's columns into every rank's buffer over NVLink and a one-warp
+peer-flag kernel signals completion; with ``gather``, an NCCL all-gather of the slabs and
+the [g][M][N/g] -> [M][N] assembly.  A step is one pass of the path over one batch:
+act-quant -> tcgen05 GEMM (-> exchange).  ``value`` is whole-job TOPS (2*M*K*N / step time, device-timed with CUDA
 events, max over ranks), inputs resident in HBM, L2 flushed between timed steps by a
 256 MiB write outside the timed region.  Scaling is strong (the layer is fixed).
 
@@ -16,7 +18,7 @@ The line also carries: the decode half of the metric (W8A8 K=2560 N=9728 at M=1,
 weights rotated through 8 copies so they come from HBM); the roofline of the dominant
 kernel; the CPU baseline (the C oracle, a bounded row sample, all host threads; rank 0,
 N=1); ``e2e`` through the reference-facing C-ABI call with host f32 buffers
-(qlinear_run_f32 at N=1; H2D -> run -> all-gather -> D2H at N>1); SM clocks sampled
+(qlinear_run_f32 at N=1; H2D -> run with the exchange -> D2H at N>1); SM clocks sampled
 during the timed region.
 
 ``--impl reference`` times the reference's CPU implementation of the path (the oracle
@@ -46,8 +48,8 @@ GEMM_TRAFFIC_BYTES = 265_384_704
 
 WORKLOADS = {
     # name: (bits, K, N, M, description)
-    "cfg4": (4, 8192, 28672, 512, "cfg4 W4A8 K8192 N28672 M512 split-N + all-gather"),
-    "cfg4_m8192": (4, 8192, 28672, 8192, "cfg4 W4A8 K8192 N28672 M8192 split-N + all-gather"),
+    "cfg4": (4, 8192, 28672, 512, "cfg4 W4A8 K8192 N28672 M512 split-N"),
+    "cfg4_m8192": (4, 8192, 28672, 8192, "cfg4 W4A8 K8192 N28672 M8192 split-N"),
     "cfg0": (4, 2560, 9728, 512, "cfg0 W4A8 gate_proj K2560 N9728 M512"),
     "cfg1": (8, 2560, 9728, 1, "cfg1 W8A8 decode K2560 N9728 M1"),
 }
@@ -62,7 +64,7 @@ def parse():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg4")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="target CPU time of the oracle baseline sample")
-    ap.add_argument("--exchange", choices=["gather", "fused"], default="gather",
+    ap.add_argument("--exchange", choices=["gather", "fused"], default="fused",
                     help="split-N output exchange at N>1: NCCL all-gather + column assembly, "
                          "or the kernels' epilogues storing into every rank's buffer")
     ap.add_argument("--no-decode", action="store_true")
@@ -384,7 +386,7 @@ def run_ours(args, rank, world, local_rank):
         "exchange_us": max(0.0, mean_step - compute_s) * 1e6,
         "note": "act-quant + GEMM device time per step (max over ranks; with the fused "
                 "exchange the GEMM includes its peer stores), without the rest of the output "
-                "exchange (all-gather + assembly, or the completion all-reduce) that `value` "
+                "exchange (all-gather + assembly, or the completion signal) that `value` "
                 "includes"}
 
     # decode half of the metric: W8A8 K2560 N9728 M=1 (HBM-bound GEMV)

@@ -177,8 +177,9 @@ QLINEAR_API int qlinear_run_device(qlinear_backend *backend, const qlinear_weigh
  * the ndev (1..8) buffers c_devs[] -- this GPU's own and the peers' (opened with
  * qlinear_peer_buffer_open) -- at row m, column col_offset + n, row stride ldc.  The stores
  * to peers cross NVLink while the kernel computes; the kernels end with a system-scope
- * fence, so a collective issued on the same stream afterwards (e.g. a one-element NCCL
- * all-reduce) tells every peer that this rank's columns are in place.  The caller must keep
+ * fence, so a signal issued on the same stream afterwards (qlinear_peer_signal_wait, or a
+ * collective such as a one-element NCCL all-reduce) tells every peer that this rank's
+ * columns are in place.  The caller must keep
  * peers from reading the destination rows until then, and from being written by a later
  * call while they still read them.  SwiGLU through the tensor-core path (rows > 8) is not
  * supported here (QLINEAR_ERR_UNSUPPORTED). */
@@ -192,13 +193,26 @@ QLINEAR_API int qlinear_run_device_scatter(qlinear_backend *backend, const qline
  * (QLINEAR_IPC_HANDLE_BYTES bytes) to ipc_handle; another process opens that handle with
  * qlinear_peer_buffer_open and gets a pointer its kernels can store to over NVLink;
  * qlinear_peer_buffer_free releases either kind (opened = 1 for a pointer from
- * qlinear_peer_buffer_open). */
+ * qlinear_peer_buffer_open).  New buffers are zero-filled. */
 #define QLINEAR_IPC_HANDLE_BYTES 64
 QLINEAR_API int qlinear_peer_buffer_create(qlinear_backend *backend, size_t bytes, void **dev_ptr,
                                            unsigned char *ipc_handle);
 QLINEAR_API int qlinear_peer_buffer_open(qlinear_backend *backend, const unsigned char *ipc_handle,
                                          void **dev_ptr);
 QLINEAR_API int qlinear_peer_buffer_free(qlinear_backend *backend, void *dev_ptr, int opened);
+
+/* Completion signal of the split-N exchange, on `stream` after this rank's
+ * qlinear_run_device_scatter: raises this rank's flag to `epoch` in every rank's signal
+ * array, then waits until all `world` flags in this GPU's array have reached `epoch`, so
+ * work queued on `stream` afterwards sees every rank's columns.  sig[r]: rank r's signal
+ * array as mapped in this process (sig[rank] = this GPU's own), a peer buffer of at least
+ * 8 * world bytes, zero at creation.  epoch: 1, 2, 3, ... -- the same sequence on every
+ * rank.  limit_ns: how long the wait may take (0: 2 s); past it the kernel records a timeout
+ * that qlinear_backend_check reports as QLINEAR_ERR_TIMEOUT, and returns.  Asynchronous;
+ * QLINEAR_ERR_PARAM for world outside 1..8 or rank outside [0, world). */
+QLINEAR_API int qlinear_peer_signal_wait(qlinear_backend *backend, void *const *sig, int world,
+                                         int rank, unsigned long long epoch,
+                                         unsigned long long limit_ns, void *stream);
 
 /* Activation quantisation alone (parity export of the int8 codes): a_dev [rows][K] ->
  * codes_dev int8 [rows][K], scales_dev f32 [rows], rowsums_dev int32 [rows] (may be NULL;

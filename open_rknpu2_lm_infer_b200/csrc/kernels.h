@@ -111,6 +111,19 @@ cudaError_t launch_gemm(const WeightView &w, const CUtensorMap &wmap, const ActV
                         const OutputSet &out,
                         int out_type, long long ldc, unsigned *err, void *sk_ws, bool pdl,
                         cudaStream_t stream);
+// The same with out.count > 1 (launch_gemm forwards to it): the split-N exchange's GEMM.
+cudaError_t launch_gemm_scatter(const WeightView &w, const CUtensorMap &wmap, const ActView &a,
+                                const CUtensorMap &amap, const GemmPlan &plan, int rows,
+                                const OutputSet &out, int out_type, long long ldc, unsigned *err,
+                                void *sk_ws, bool pdl, cudaStream_t stream);
+
+// Signal arrays of the split-N exchange's ranks (peer_sync.cu): sig[r] = rank r's, mapped here.
+struct PeerSignals {
+    void *sig[kMaxOutputs];
+    int world, rank;
+};
+cudaError_t launch_peer_signal_wait(const PeerSignals &s, unsigned long long epoch, unsigned *err,
+                                    unsigned long long limit_ns, cudaStream_t stream);
 
 // Failure-path self-test: one warp waits limit_ns on an mbarrier nobody arrives on, then
 // records QL_DEVERR_TIMEOUT in *err and returns.

@@ -629,6 +629,11 @@ int qlinear_peer_buffer_create(qlinear_backend *b, size_t bytes, void **dev_ptr,
         return cuda_status(e);
     }
     static_assert(sizeof(h) == QLINEAR_IPC_HANDLE_BYTES, "CUDA IPC handle size");
+    const cudaError_t z = cudaMemset(p, 0, bytes);  // signal arrays start at epoch 0
+    if (z != cudaSuccess) {
+        cudaFree(p);
+        return cuda_status(z);
+    }
     std::memcpy(ipc_handle, &h, sizeof(h));
     *dev_ptr = p;
     return QLINEAR_OK;
@@ -804,6 +809,25 @@ int qlinear_backend_check(qlinear_backend *b, void *stream) {
         reset_after_timeout(b);
         return QLINEAR_ERR_TIMEOUT;
     }
+    return QLINEAR_OK;
+}
+
+int qlinear_peer_signal_wait(qlinear_backend *b, void *const *sig, int world, int rank,
+                             unsigned long long epoch, unsigned long long limit_ns,
+                             void *stream) {
+    if (!b || !sig || world < 1 || world > kMaxOutputs || rank < 0 || rank >= world)
+        return QLINEAR_ERR_PARAM;
+    PeerSignals s{};
+    for (int r = 0; r < world; r++) {
+        if (!sig[r]) return QLINEAR_ERR_PARAM;
+        s.sig[r] = sig[r];
+    }
+    s.world = world;
+    s.rank = rank;
+    DeviceGuard guard(b->device);
+    QL_TRY(launch_peer_signal_wait(s, epoch, b->d_err, limit_ns ? limit_ns : QL_WAIT_NS,
+                                   static_cast<cudaStream_t>(stream)));
+    b->launches++;
     return QLINEAR_OK;
 }
 

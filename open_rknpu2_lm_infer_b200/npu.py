@@ -210,6 +210,16 @@ class Backend:
         _check(self._lib.qlinear_peer_buffer_free(self.raw, ptr, 1 if opened else 0),
                "peer buffer free")
 
+    def peer_signal_wait(self, sig, rank: int, epoch: int, limit_s: float = 0.0,
+                         stream=None) -> None:
+        """qlinear_peer_signal_wait: raise this rank's flag to `epoch` in every rank's signal
+        array (`sig`: device addresses in rank order, this GPU's own at `rank`) and wait on
+        `stream` until every rank's flag here has reached it (0 s limit: the default 2 s)."""
+        arr = (ctypes.c_void_p * len(sig))(*[int(p) for p in sig])
+        _check(self._lib.qlinear_peer_signal_wait(self.raw, arr, len(sig), rank, epoch,
+                                                  int(limit_s * 1e9), stream),
+               "peer signal wait")
+
     def selftest_wait_timeout(self, limit_s: float = 0.2) -> int:
         """Run the failure-path self-test (a bounded wait that nothing satisfies); returns the
         status, QLINEAR_ERR_TIMEOUT when the path works."""

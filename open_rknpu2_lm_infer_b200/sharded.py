@@ -11,8 +11,9 @@ single-GPU run.  Two ways to put the [M][N] output together on every rank:
 * ``run_exchange`` (``fused_exchange=True``): the kernels' epilogues store each rank's
   columns straight into every rank's ``[M][N]`` exchange buffer over NVLink while they
   compute (``qlinear_run_device_scatter``; the buffers are shared through CUDA IPC,
-  ``qlinear_peer_buffer_*``), and a one-element all-reduce afterwards tells every rank the
-  output is complete.  No gather, no assembly pass.
+  ``qlinear_peer_buffer_*``), then a one-warp kernel raises this rank's flag in every rank's
+  signal array and waits for all of them (``qlinear_peer_signal_wait``), so the output is
+  complete on every rank.  No gather, no assembly pass, no collective per call.
 
 The reference is single-device; this has no counterpart there.
 """
@@ -66,7 +67,8 @@ class ShardedLinear:
         self._bufs = {}
         self._xbufs = {}  # output dtype -> (own ptr, peer ptrs, [max_rows][N] view, type code)
         self._default_dtype = None
-        self._flag = None
+        self._sig = None    # signal arrays in rank order (this rank's own at self.rank)
+        self._epoch = 0
         if fused_exchange:
             self.add_exchange(max_rows, out_dtype)
 
@@ -94,8 +96,12 @@ class ShardedLinear:
         self._xbufs[dtype] = (ptr, peers, view, L.F16 if dtype == torch.float16 else L.F32)
         if self._default_dtype is None:
             self._default_dtype = dtype
-        if self._flag is None:
-            self._flag = torch.zeros(1, dtype=torch.float32, device=dev)
+        if self._sig is None:
+            sptr, shandle = self.backend.peer_buffer_create(8 * self.world)
+            shandles = [None] * self.world
+            dist.all_gather_object(shandles, shandle, group=self.group)
+            self._sig = [sptr if r == self.rank else self.backend.peer_buffer_open(h)
+                         for r, h in enumerate(shandles)]
 
     @property
     def output(self):
@@ -103,10 +109,10 @@ class ShardedLinear:
 
     def run_exchange(self, a, rows: int, stream=None, out_dtype=None):
         """Fused split-N: this rank's columns go straight into every rank's exchange buffer of
-        out_dtype; returns the [rows][N] output (this rank's buffer), complete on every rank
-        once the call's collective is done on the stream.  The caller keeps every rank from
-        reading the previous output while a new call writes it."""
-        import torch.distributed as dist
+        out_dtype; returns the [rows][N] output (this rank's buffer), complete for the work
+        queued on `stream` after the call.  Every rank makes the same calls in the same order
+        (the signal epochs must match).  The caller keeps every rank from reading the previous
+        output while a new call writes it."""
         key = out_dtype or self._default_dtype
         if key not in self._xbufs:
             raise RuntimeError("no exchange buffer for this output type (add_exchange)")
@@ -115,19 +121,28 @@ class ShardedLinear:
             raise ValueError("rows out of range for the exchange buffer")
         self.linear.run_device_scatter(a, [own] + peers, out_type, self.n, self.lo, rows,
                                        stream=stream)
-        dist.all_reduce(self._flag, group=self.group)
+        self._epoch += 1
+        self.backend.peer_signal_wait(self._sig, self.rank, self._epoch, stream=stream)
         return view[:rows]
 
     def close(self) -> None:
+        """Collective: every rank unmaps its peers' buffers, then frees its own."""
+        import torch
         import torch.distributed as dist
         if self._xbufs:
+            torch.cuda.synchronize(self.backend.device)  # no exchange kernel in flight
             for own, peers, _, _ in self._xbufs.values():
                 for p in peers:
+                    self.backend.peer_buffer_free(p, True)
+            for r, p in enumerate(self._sig):
+                if r != self.rank:
                     self.backend.peer_buffer_free(p, True)
             dist.barrier(group=self.group)  # every peer unmapped this rank's buffers
             for own, _, _, _ in self._xbufs.values():
                 self.backend.peer_buffer_free(own, False)
+            self.backend.peer_buffer_free(self._sig[self.rank], False)
             self._xbufs = {}
+            self._sig = None
         self.linear.close()
 
     def _buf(self, key, shape, dtype, device):
