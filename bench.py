@@ -42,9 +42,9 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 # DRAM traffic of the dominant kernel per launch on the default workload
-# (dram__bytes_read.sum + dram__bytes_write.sum = 246.35 MB + 19.03 MB) from the ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum = 246.04 MB + 18.01 MB) from the ncu capture
 # summarised in profiles/gemm_w4a8_cfg4_m512.md (same workload, one GPU).
-GEMM_TRAFFIC_BYTES = 265_384_704
+GEMM_TRAFFIC_BYTES = 264_049_408
 
 WORKLOADS = {
     # name: (bits, K, N, M, description)

@@ -39,6 +39,16 @@ GemmPlan plan_gemm(const WeightView &w, int rows, int max_pairs, bool allow_sk) 
     const int tiles_m = std::max(1, (rows + 255) / 256);
     int tok = (rows + tiles_m - 1) / tiles_m;
     tok = std::max(32, (tok + 31) / 32 * 32);  // 2-CTA MMA: N multiple of 32
+    // A narrow weight shard (split-N over many GPUs) leaves pairs idle: halve the token tile
+    // while twice the tiles still run in one wave on the pairs (not below 64 tokens, where
+    // the weight operand's shared-memory traffic per multiply-accumulate starts to bound the
+    // MMA).  cfg4 at M=512 on 8 GPUs: 28 tiles of 256 tokens -> 56 of 128 on 74 pairs.
+    {
+        const long long ch_tiles = (w.Np + CHT - 1) / CHT;
+        while (tok >= 128 && tok % 64 == 0 &&
+               ch_tiles * ((rows + tok / 2 - 1) / (tok / 2)) <= std::max(1, max_pairs))
+            tok /= 2;
+    }
     plan.tok = tok;
     const int stage_bytes = (tok / 2) * KB + A_SLOT;
     const int fixed = SMEM_RESERVE;

@@ -129,6 +129,8 @@ def test_odd_shape(backend, golden):
     (4, 8192, 1024, 8),     # cfg4 K, N slice (decode)
     (4, 8192, 1024, 300),   # cfg4 K, N slice, ragged token tiles
     (8, 4096, 2560, 77),    # o_proj shape, odd rows
+    (8, 1024, 3584, 512),   # cfg4's N/8 shard width: 256-token tiles halved to 128
+    (4, 512, 1024, 512),    # narrower still: halved twice, 64-token tiles
 ])
 def test_seeded_config_shapes_fp16(backend, coracle, bits, k, n, rows):
     w = W.weight_codes(bits, k, n, stream=bits)
