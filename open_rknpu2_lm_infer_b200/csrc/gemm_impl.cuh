@@ -84,10 +84,11 @@ struct GemmArgs {
     int tok, stages, n_tok_tiles, num_tiles;
     uint32_t tmem_cols;
     unsigned *err;
-    int sk;              // 1: stream-K schedule, 0: whole tiles strided over the pairs
-    int sk_tiles;        // stream-K: the last sk_tiles tiles are split, the others whole
+    int sk;              // 1: stream-K; 2: tail split; 0: whole tiles strided over the pairs
+    int sk_tiles;        // stream-K / tail split: the last sk_tiles tiles are split, the
+                         // others whole
     long long units;     // stream-K: (channel tile, k-block) iterations of one token tile
-                         // in the split region
+                         // in the split region; tail split: sub-tiles per split tile
     int32_t *sk_ws;      // stream-K partial sums [pairs][left | right][tok][256]
     int *sk_cnt;         // contributions per (slot, epilogue sub-block) [256][16], zero
                          // between launches
@@ -108,12 +109,18 @@ struct GemmArgs {
 // which pair finishes first).  The split region comes last on purpose: measured on B200,
 // the loads that sum a split tile wait behind the TMA weight stream for tens of
 // microseconds while the main loops run, and are quick once it has ended.
+//
+// Tail split (sk == 2): the whole tiles are the first num_tiles - sk_tiles, a whole number of
+// waves; each of the last sk_tiles tiles is cut along its tokens into `units` sub-tiles of
+// tok / units tokens (whole k-loop each), sub-tile j going to pair j, so the last partial
+// wave of big tiles becomes one short wave of small ones on otherwise idle pairs.  Sub-tile
+// j is reported as t = num_tiles + j (tile_geom gives its coordinates).
 struct Sched {
     long long u, end;  // split-region iterations still to walk
-    int t_dp, dp_end, step, nkb, ntt, g, base;
+    int t_dp, dp_end, step, nkb, ntt, g, base, tail;
     __device__ Sched(const GemmArgs &p, int cid, int ncl)
-        : t_dp(cid), step(ncl), nkb(p.nkb), ntt(p.n_tok_tiles) {
-        if (p.sk) {
+        : t_dp(cid), step(ncl), nkb(p.nkb), ntt(p.n_tok_tiles), tail(-1) {
+        if (p.sk == 1) {
             const int pg = ncl / ntt, i = cid / ntt;
             g = cid % ntt;
             u = p.units * i / pg;
@@ -123,6 +130,10 @@ struct Sched {
             g = base = 0;
             u = end = 0;
             dp_end = p.num_tiles;
+            if (p.sk == 2) {
+                dp_end = p.num_tiles - p.sk_tiles;
+                if ((long long)cid < (long long)p.sk_tiles * p.units) tail = p.num_tiles + cid;
+            }
         }
     }
     __device__ bool next(int &t, int &kb0, int &kb1) {
@@ -131,6 +142,13 @@ struct Sched {
             kb0 = 0;
             kb1 = nkb;
             t_dp += step;
+            return true;
+        }
+        if (tail >= 0) {
+            t = tail;
+            kb0 = 0;
+            kb1 = nkb;
+            tail = -1;
             return true;
         }
         if (u >= end) return false;
@@ -143,6 +161,22 @@ struct Sched {
         return true;
     }
 };
+
+// Coordinates of work item t (Sched::next): channel tile tc, first token tok0, tokens ntok
+// (the MMA's N).
+__device__ __forceinline__ void tile_geom(const GemmArgs &p, int t, int &tc, int &tok0, int &ntok) {
+    if (t < p.num_tiles) {
+        tc = t / p.n_tok_tiles;
+        tok0 = (t - tc * p.n_tok_tiles) * p.tok;
+        ntok = p.tok;
+    } else {  // tail sub-tile j of split tile num_tiles - sk_tiles + j / units
+        const int j = t - p.num_tiles, split = (int)p.units;
+        const int tile = p.num_tiles - p.sk_tiles + j / split;
+        tc = tile / p.n_tok_tiles;
+        ntok = p.tok / split;
+        tok0 = (tile - tc * p.n_tok_tiles) * p.tok + (j % split) * ntok;
+    }
+}
 
 // The same sequence one k-block at a time.
 struct Units {
@@ -205,7 +239,8 @@ __device__ __forceinline__ uint64_t smem_desc_sw128_k(const void *tile) {
 template <int BITS, typename OutT, int NDST>
 __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap amap,
-                const GemmArgs p, const OutputSet outs) {
+                const GemmArgs p, const OutputSet outs,
+                const __grid_constant__ CUtensorMap amap_sub) {
     constexpr bool SCATTER = NDST > 1;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -250,6 +285,7 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&wmap);
         tma_prefetch_desc(&amap);
+        if (p.sk == 2) tma_prefetch_desc(&amap_sub);
     }
     if (warp == 1) {
         tmem_alloc_pair(tmem_slot, p.tmem_cols);
@@ -264,17 +300,16 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
     const uint32_t full0 = map_to_rank(&full[0], 0);  // leader's barriers (cluster addresses)
     const uint32_t afull0 = map_to_rank(&afull[0], 0);
     const uint32_t acce0 = map_to_rank(&acce[0], 0);
-    // bytes the leader's `full` barrier receives per stage from both CTAs
-    const uint32_t tx_pair = 2u * (uint32_t)(b_half + (BITS == 8 ? A_SLOT : 0));
 
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
-            auto load_weights = [&](int s, int kb, int tc) {
+            // tx: the bytes the leader's `full` barrier receives for the stage from both CTAs
+            auto load_weights = [&](int s, int kb, int tc, uint32_t tx) {
                 if (BITS == 8)
                     tma_load_2d_pair(sW + s * w_slot, &wmap, full0 + 8u * s, kb * KB,
                                      tc * CHT + (int)rank * CH_CTA);
-                if (rank == 0) mbar_arrive_expect_tx(&full[s], tx_pair);
+                if (rank == 0) mbar_arrive_expect_tx(&full[s], tx);
             };
             // Weight tiles of the first stages do not depend on the preceding kernel:
             // issue them before waiting for it.
@@ -282,8 +317,12 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
             {
                 Sched sp(p, (int)cid, (int)ncl);
                 int t, kb0, kb1;
-                while (pre < S && sp.next(t, kb0, kb1))
-                    for (int kb = kb0; kb < kb1 && pre < S; kb++) load_weights(pre++, kb, t / p.n_tok_tiles);
+                while (pre < S && sp.next(t, kb0, kb1)) {
+                    int tc, tok0, ntok;
+                    tile_geom(p, t, tc, tok0, ntok);
+                    const uint32_t tx = 2u * (uint32_t)((ntok / 2) * KB + (BITS == 8 ? A_SLOT : 0));
+                    for (int kb = kb0; kb < kb1 && pre < S; kb++) load_weights(pre++, kb, tc, tx);
+                }
             }
             grid_dep_wait();
             uint32_t it = 0, s = 0, ph = 0;  // iteration, stage, stage phase
@@ -291,14 +330,18 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
             Sched sp(p, (int)cid, (int)ncl);
             int t, kb0, kb1;
             while (ok && sp.next(t, kb0, kb1)) {
-                const int tc = t / p.n_tok_tiles, tt = t % p.n_tok_tiles;
+                int tc, tok0, ntok;
+                tile_geom(p, t, tc, tok0, ntok);
+                // a tail sub-tile loads only its own activation rows (a box of ntok/2 rows)
+                const CUtensorMap *am = ntok == tok ? &amap : &amap_sub;
+                const uint32_t tx = 2u * (uint32_t)((ntok / 2) * KB + (BITS == 8 ? A_SLOT : 0));
                 for (int kb = kb0; kb < kb1; kb++, it++) {
                     if (it >= (uint32_t)pre) {
                         if (!(ok = mbar_wait(&empty[s], ph ^ 1, err, abort_flag))) break;
-                        load_weights(s, kb, tc);
+                        load_weights(s, kb, tc, tx);
                     }
-                    tma_load_2d_pair(sB + s * b_half, &amap, full0 + 8u * s, kb * KB,
-                                     tt * tok + (int)rank * (tok / 2));
+                    tma_load_2d_pair(sB + s * b_half, am, full0 + 8u * s, kb * KB,
+                                     tok0 + (int)rank * (ntok / 2));
                     if (++s == (uint32_t)S) { s = 0; ph ^= 1; }
                 }
             }
@@ -315,7 +358,6 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer (leader)
         if (lane == 0 && rank == 0) {
-            const uint32_t idesc = idesc_i8(2 * CH_CTA, tok, BITS == 8, true);
             uint32_t s = 0, ph = 0, local = 0;
             bool ok = true;
             Sched sm(p, (int)cid, (int)ncl);
@@ -325,6 +367,9 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                 if (!(ok = mbar_wait(&acce[ab], ((local >> 1) & 1) ^ 1, err, abort_flag))) break;
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(ab * tok);
+                int tc, tok0, ntok;
+                tile_geom(p, t, tc, tok0, ntok);
+                const uint32_t idesc = idesc_i8(2 * CH_CTA, ntok, BITS == 8, true);
                 for (int kb = kb0; kb < kb1; kb++) {
                     if (!(ok = mbar_wait(&full[s], ph, err, abort_flag))) break;
                     if (BITS == 4 && !(ok = mbar_wait(&afull[s], ph, err, abort_flag))) break;
@@ -350,7 +395,6 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
         grid_dep_wait();  // the activation scales / row sums come from the previous kernel
         const int q = warp & 3;                 // TMEM lane quadrant this warp may access
         const int colh = (warp - 2) >> 2;       // which half of the tok columns
-        const int cols = tok / 2;               // <= 128: at most 8 chunks of 16 columns
         const int sub = (int)rank * EPI_WARPS + (warp - 2);  // this warp's part of a tile
         const int chl = (int)rank * CH_CTA + q * 32 + lane;  // channel within the tile
         uint32_t local = 0;
@@ -358,7 +402,7 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
         // column c of the warp's range sits in lane c % 32 of register c / 32.
         float sa_r[4];
         int rs_r[4];
-        auto load_scales = [&](int tok_base) {
+        auto load_scales = [&](int tok_base, int cols) {
 #pragma unroll
             for (int i = 0; i < 4; i++) {
                 const int m = tok_base + i * 32 + lane;
@@ -409,11 +453,13 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                 }
             }
         };
-        const int pg = p.sk ? (int)ncl / p.n_tok_tiles : 1;  // stream-K pairs per group
+        const int pg = p.sk == 1 ? (int)ncl / p.n_tok_tiles : 1;  // stream-K pairs per group
         Sched se(p, (int)cid, (int)ncl);
         int t, kb0, kb1;
         for (; se.next(t, kb0, kb1); local++) {
-            const int tc = t / p.n_tok_tiles, tt = t % p.n_tok_tiles;
+            int tc, tok0, ntok;
+            tile_geom(p, t, tc, tok0, ntok);
+            const int cols = ntok / 2;  // this warp's columns: <= 128, at most 8 chunks of 16
             const int ab = local & 1;
             // every lane waits (bounded); the warp leaves together if any lane gave up,
             // so the warp-collective tcgen05.ld / shuffles below stay converged
@@ -422,13 +468,13 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
             tc_fence_after();
             const int ch = tc * CHT + chl;
             const bool chv = ch < p.N;
-            const int tok_base = tt * tok + colh * cols;
+            const int tok_base = tok0 + colh * cols;
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) +
                                    (uint32_t)(ab * tok + colh * cols);
             if (kb0 == 0 && kb1 == p.nkb) {
                 // the whole tile: dequantise from tensor memory
                 const float sw = chv ? p.wscale[ch] : 0.0f;
-                load_scales(tok_base);
+                load_scales(tok_base, cols);
 #pragma unroll
                 for (int cc = 0; cc < 8; cc++) {
                     if (cc * 16 >= cols) break;
@@ -478,7 +524,7 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
             if (!last) continue;
             __threadfence();
             const float sw = chv ? p.wscale[ch] : 0.0f;
-            load_scales(tok_base);
+            load_scales(tok_base, cols);
             // the tile's buffers: left of b_f, right of b_f .. b_f + nseg - 2.  Two chunks at
             // a time, the loads of both first buffers issued together: under the main loops'
             // traffic an L2 round trip costs microseconds, so the number of dependent
@@ -531,7 +577,9 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
             const long long row_bytes = (long long)p.nkb * (KB / 2);
             // Packed codes of iteration (tile t, k-block kb) for this thread's 4 rows.
             auto fetch = [&](uint4 (&b)[4], int t, int kb) {
-                const int n0 = (t / p.n_tok_tiles) * CHT + (int)rank * CH_CTA;
+                int tc, tok0, ntok;
+                tile_geom(p, t, tc, tok0, ntok);
+                const int n0 = tc * CHT + (int)rank * CH_CTA;
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
                     const int n = n0 + r0 + 32 * j;
@@ -606,7 +654,8 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
 }
 
 template <int BITS, typename OutT, int NDST>
-cudaError_t launch_s(const CUtensorMap &wmap, const CUtensorMap &amap, const GemmArgs &args,
+cudaError_t launch_s(const CUtensorMap &wmap, const CUtensorMap &amap,
+                     const CUtensorMap &amap_sub, const GemmArgs &args,
                      const OutputSet &outs, const GemmPlan &plan, bool pdl,
                      cudaStream_t stream) {
     auto kern = gemm_kernel<BITS, OutT, NDST>;
@@ -637,7 +686,7 @@ cudaError_t launch_s(const CUtensorMap &wmap, const CUtensorMap &amap, const Gem
     attr[1].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, kern, wmap, amap, args, outs);
+    return cudaLaunchKernelEx(&cfg, kern, wmap, amap, args, outs, amap_sub);
 }
 
 // The kernel's arguments for a launch (the output pointer is set by the caller).
@@ -662,8 +711,13 @@ inline GemmArgs make_args(const WeightView &w, const ActView &a, const GemmPlan 
     args.tmem_cols = cols;
     args.err = err;
     args.sk_tiles = plan.sk_tiles;
+    if (plan.sk == 2) {  // tail split: sub-tiles per split tile, no workspace
+        args.sk = 2;
+        args.units = plan.split;
+        return args;
+    }
     args.units = (long long)(plan.sk_tiles / args.n_tok_tiles) * args.nkb;
-    args.sk = plan.sk && sk_ws && plan.grid / 2 <= SK_MAX_PAIRS ? 1 : 0;
+    args.sk = plan.sk == 1 && sk_ws && plan.grid / 2 <= SK_MAX_PAIRS ? 1 : 0;
     if (args.sk) {
         args.sk_cnt = static_cast<int *>(sk_ws);
         args.sk_ws = reinterpret_cast<int32_t *>(static_cast<char *>(sk_ws) + SK_CNT_BYTES);
@@ -673,17 +727,18 @@ inline GemmArgs make_args(const WeightView &w, const ActView &a, const GemmPlan 
 
 // Launches the NDST-destination kernel for the weights' bits and the output type.
 template <int NDST>
-cudaError_t launch_n(const CUtensorMap &wmap, const CUtensorMap &amap, const GemmArgs &args,
+cudaError_t launch_n(const CUtensorMap &wmap, const CUtensorMap &amap,
+                     const CUtensorMap &amap_sub, const GemmArgs &args,
                      const OutputSet &outs, const GemmPlan &plan, int bits, int out_type, bool pdl,
                      cudaStream_t stream) {
     if (bits == 8) {
-        if (out_type == kF16) return launch_s<8, __half, NDST>(wmap, amap, args, outs, plan, pdl, stream);
-        if (out_type == kF32) return launch_s<8, float, NDST>(wmap, amap, args, outs, plan, pdl, stream);
-        return launch_s<8, int32_t, NDST>(wmap, amap, args, outs, plan, pdl, stream);
+        if (out_type == kF16) return launch_s<8, __half, NDST>(wmap, amap, amap_sub, args, outs, plan, pdl, stream);
+        if (out_type == kF32) return launch_s<8, float, NDST>(wmap, amap, amap_sub, args, outs, plan, pdl, stream);
+        return launch_s<8, int32_t, NDST>(wmap, amap, amap_sub, args, outs, plan, pdl, stream);
     }
-    if (out_type == kF16) return launch_s<4, __half, NDST>(wmap, amap, args, outs, plan, pdl, stream);
-    if (out_type == kF32) return launch_s<4, float, NDST>(wmap, amap, args, outs, plan, pdl, stream);
-    return launch_s<4, int32_t, NDST>(wmap, amap, args, outs, plan, pdl, stream);
+    if (out_type == kF16) return launch_s<4, __half, NDST>(wmap, amap, amap_sub, args, outs, plan, pdl, stream);
+    if (out_type == kF32) return launch_s<4, float, NDST>(wmap, amap, amap_sub, args, outs, plan, pdl, stream);
+    return launch_s<4, int32_t, NDST>(wmap, amap, amap_sub, args, outs, plan, pdl, stream);
 }
 
 }  // namespace

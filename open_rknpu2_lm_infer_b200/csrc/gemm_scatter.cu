@@ -6,7 +6,8 @@
 namespace ql {
 
 cudaError_t launch_gemm_scatter(const WeightView &w, const CUtensorMap &wmap, const ActView &a,
-                                const CUtensorMap &amap, const GemmPlan &plan, int rows,
+                                const CUtensorMap &amap, const CUtensorMap &amap_sub,
+                                const GemmPlan &plan, int rows,
                                 const OutputSet &out, int out_type, long long ldc, unsigned *err,
                                 void *sk_ws, bool pdl, cudaStream_t stream) {
     if (out.count < 2 || out.count > kMaxOutputs) return cudaErrorInvalidValue;
@@ -17,9 +18,9 @@ cudaError_t launch_gemm_scatter(const WeightView &w, const CUtensorMap &wmap, co
     OutputSet o = out;
     for (int d = out.count; d < n; d++) o.dst[d] = out.dst[0];
     o.count = n;
-    if (n == 2) return launch_n<2>(wmap, amap, args, o, plan, w.bits, out_type, pdl, stream);
-    if (n == 4) return launch_n<4>(wmap, amap, args, o, plan, w.bits, out_type, pdl, stream);
-    return launch_n<8>(wmap, amap, args, o, plan, w.bits, out_type, pdl, stream);
+    if (n == 2) return launch_n<2>(wmap, amap, amap_sub, args, o, plan, w.bits, out_type, pdl, stream);
+    if (n == 4) return launch_n<4>(wmap, amap, amap_sub, args, o, plan, w.bits, out_type, pdl, stream);
+    return launch_n<8>(wmap, amap, amap_sub, args, o, plan, w.bits, out_type, pdl, stream);
 }
 
 }  // namespace ql

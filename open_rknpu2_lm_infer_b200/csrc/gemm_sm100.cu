@@ -89,29 +89,49 @@ GemmPlan plan_gemm(const WeightView &w, int rows, int max_pairs, bool allow_sk) 
             plan.sk_tiles = (int)(plan.tiles - whole * sk_pairs);
         }
     }
-    const int pairs = plan.sk ? (int)(group * n_tok_tiles) : dp_pairs;
+    // Tail split: R tiles left for a last partial wave of whole tiles (at most half the
+    // pairs busy) are each cut along their tokens into S sub-tiles (S a power of two, S*R
+    // pairs, >= 32 tokens each) that run at once on otherwise idle pairs.  Each sub-tile
+    // still streams its tile's whole weight block, but from L2 after the first.  cfg4 at
+    // M=512: 224 tiles on 74 pairs = 3 waves + 2 tiles; the 2 tiles become 16 sub-tiles of
+    // 32 tokens.
+    plan.split = 1;
+    if (!plan.sk && plan.tiles > maxp) {
+        const int R = plan.tiles % maxp;
+        int S = 1;
+        while (R > 0 && 2 * S * R <= maxp && tok / (2 * S) >= 32 && (tok / (2 * S)) % 32 == 0)
+            S *= 2;
+        if (S > 1) {
+            plan.sk = 2;
+            plan.sk_tiles = R;
+            plan.split = S;
+        }
+    }
+    const int pairs = plan.sk == 1 ? (int)(group * n_tok_tiles) : dp_pairs;
     plan.grid = 2 * pairs;
     return plan;
 }
 
 size_t gemm_sk_bytes(const GemmPlan &plan) {
-    if (!plan.sk) return 0;
+    if (plan.sk != 1) return 0;
     const size_t pairs = (size_t)plan.grid / 2;
     return SK_CNT_BYTES + 2 * pairs * (size_t)plan.tok * CHT * sizeof(int32_t);
 }
 
 cudaError_t launch_gemm(const WeightView &w, const CUtensorMap &wmap, const ActView &a,
-                        const CUtensorMap &amap, const GemmPlan &plan, int rows,
+                        const CUtensorMap &amap, const CUtensorMap &amap_sub,
+                        const GemmPlan &plan, int rows,
                         const OutputSet &out, int out_type, long long ldc, unsigned *err,
                         void *sk_ws, bool pdl, cudaStream_t stream) {
     if (out.count < 1 || out.count > kMaxOutputs) return cudaErrorInvalidValue;
     if (out.count > 1)
-        return launch_gemm_scatter(w, wmap, a, amap, plan, rows, out, out_type, ldc, err, sk_ws,
+        return launch_gemm_scatter(w, wmap, a, amap, amap_sub, plan, rows, out, out_type, ldc,
+                                   err, sk_ws,
                                    pdl, stream);
     GemmArgs args = make_args(w, a, plan, rows, ldc, err, sk_ws);
     // one destination: p.out, offset by the column offset
     args.out = static_cast<char *>(out.dst[0]) + out.col0 * (out_type == kF16 ? 2 : 4);
-    return launch_n<1>(wmap, amap, args, out, plan, w.bits, out_type, pdl, stream);
+    return launch_n<1>(wmap, amap, amap_sub, args, out, plan, w.bits, out_type, pdl, stream);
 }
 
 }  // namespace ql

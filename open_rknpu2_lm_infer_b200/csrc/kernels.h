@@ -91,8 +91,11 @@ struct GemmPlan {
     int grid;       // persistent CTAs
     int tiles;
     int sk;         // 1: stream-K (every pair the same number of k-blocks, split tiles
-                    //    summed in a workspace), 0: whole tiles strided over the pairs
-    int sk_tiles;   // stream-K: the split region, the last sk_tiles tiles
+                    //    summed in a workspace); 2: tail split (the last partial wave's
+                    //    tiles cut along their tokens into `split` sub-tiles on idle
+                    //    pairs); 0: whole tiles strided over the pairs
+    int sk_tiles;   // stream-K / tail split: the last sk_tiles tiles
+    int split;      // tail split: sub-tiles per split tile
 };
 // max_pairs: gemm_pair_capacity() of the device (CTA pairs resident at once); allow_sk: the
 // plan may choose the stream-K schedule (QLINEAR_BACKEND_GEMM_STREAM_K).
@@ -107,13 +110,15 @@ size_t gemm_sk_bytes(const GemmPlan &plan);
 // griddepcontrol.wait before reading the activation codes / scales).  sk_ws: the zeroed
 // stream-K workspace of gemm_sk_bytes(plan) bytes (ignored without stream-K).
 cudaError_t launch_gemm(const WeightView &w, const CUtensorMap &wmap, const ActView &a,
-                        const CUtensorMap &amap, const GemmPlan &plan, int rows,
+                        const CUtensorMap &amap, const CUtensorMap &amap_sub,
+                        const GemmPlan &plan, int rows,
                         const OutputSet &out,
                         int out_type, long long ldc, unsigned *err, void *sk_ws, bool pdl,
                         cudaStream_t stream);
 // The same with out.count > 1 (launch_gemm forwards to it): the split-N exchange's GEMM.
 cudaError_t launch_gemm_scatter(const WeightView &w, const CUtensorMap &wmap, const ActView &a,
-                                const CUtensorMap &amap, const GemmPlan &plan, int rows,
+                                const CUtensorMap &amap, const CUtensorMap &amap_sub,
+                                const GemmPlan &plan, int rows,
                                 const OutputSet &out, int out_type, long long ldc, unsigned *err,
                                 void *sk_ws, bool pdl, cudaStream_t stream);
 

@@ -345,21 +345,27 @@ int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_
     const CUtensorMap &gmap = use8 ? w->wmap8 : w->wmap;
     const GemmPlan plan = plan_gemm(gv, rows, pairs, (b->flags & QLINEAR_BACKEND_GEMM_STREAM_K) != 0);
     if ((st = ensure_sk(b, gemm_sk_bytes(plan)))) return st;
-    if (plan.sk) b->gemm_stream_k_calls++;
+    if (plan.sk == 1) b->gemm_stream_k_calls++;
     const CUtensorMap *amap = nullptr;
     st = get_amap(b, v.Kp, plan.tok, &amap);
     if (st) return st;
+    // the tail split's sub-tiles load a box of their own rows
+    const CUtensorMap *amap_sub = amap;
+    if (plan.sk == 2) {
+        st = get_amap(b, v.Kp, plan.tok / plan.split, &amap_sub);
+        if (st) return st;
+    }
     if (!swiglu) {
-        QL_TRY(launch_gemm(gv, gmap, av, *amap, plan, rows, outs, c_type, ldc, b->d_err, b->d_sk,
-                           true, stream));
+        QL_TRY(launch_gemm(gv, gmap, av, *amap, *amap_sub, plan, rows, outs, c_type, ldc,
+                           b->d_err, b->d_sk, true, stream));
         b->launches++;
     } else {
         st = ensure_dev(reinterpret_cast<void **>(&b->d_y), &b->y_elems,
                         (size_t)rows * v.N * sizeof(float));
         if (st) return st;
         if (outs.count != 1) return QLINEAR_ERR_UNSUPPORTED;  // the SwiGLU pass writes one buffer
-        QL_TRY(launch_gemm(gv, gmap, av, *amap, plan, rows, single_output(b->d_y), kF32, v.N,
-                           b->d_err, b->d_sk, true, stream));
+        QL_TRY(launch_gemm(gv, gmap, av, *amap, *amap_sub, plan, rows, single_output(b->d_y), kF32,
+                           v.N, b->d_err, b->d_sk, true, stream));
         QL_TRY(launch_swiglu(b->d_y, rows, v.N, c_dev, c_type, ldc, stream));
         b->launches += 2;
     }

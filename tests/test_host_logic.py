@@ -208,3 +208,75 @@ def test_stream_k_schedule_covers_every_iteration_once():
             if nseg > 1:
                 assert 0 <= slot < P and slot not in slots
                 slots.add(slot)
+
+
+# Restatement of the GEMM's token-tile choice and tail split (csrc/gemm_sm100.cu plan_gemm,
+# csrc/gemm_impl.cuh Sched / tile_geom), with the same integer formulas: the token tile from
+# the row count, halved for narrow shards while twice the tiles fit in one wave; whole tiles
+# strided over the pairs; the R tiles of a last partial wave (at most half the pairs) each cut
+# into S sub-tiles of tok / S tokens, sub-tile j on pair j.  Every (channel tile, token) is
+# computed exactly once, over the whole k-loop, and every sub-tile is >= 32 tokens.
+
+def _plan_tok(rows, np_, maxp):
+    tiles_m = max(1, (rows + 255) // 256)
+    tok = (rows + tiles_m - 1) // tiles_m
+    tok = max(32, (tok + 31) // 32 * 32)
+    ch_tiles = (np_ + 255) // 256
+    while tok >= 128 and tok % 64 == 0 and ch_tiles * ((rows + tok // 2 - 1) // (tok // 2)) <= maxp:
+        tok //= 2
+    ntt = (rows + tok - 1) // tok
+    tiles = ch_tiles * ntt
+    R, S = 0, 1
+    if tiles > maxp:
+        R = tiles % maxp
+        while R > 0 and 2 * S * R <= maxp and tok // (2 * S) >= 32 and (tok // (2 * S)) % 32 == 0:
+            S *= 2
+    return tok, ntt, tiles, (R if S > 1 else 0), S
+
+
+def _tail_items(tiles, sk_tiles, split, P, cid):
+    t = cid
+    while t < tiles - sk_tiles:
+        yield t
+        t += P
+    if cid < sk_tiles * split:
+        yield tiles + cid
+
+
+def _tile_geom(t, tiles, ntt, tok, sk_tiles, split):
+    if t < tiles:
+        tc = t // ntt
+        return tc, (t - tc * ntt) * tok, tok
+    j = t - tiles
+    tile = tiles - sk_tiles + j // split
+    tc = tile // ntt
+    ntok = tok // split
+    return tc, (tile - tc * ntt) * tok + (j % split) * ntok, ntok
+
+
+def test_token_tile_and_tail_split_cover_every_token_once():
+    import random
+    rng = random.Random(11)
+    # (rows, Np, pairs): cfg4 M=512 on 1 and 8 GPUs, cfg0, ragged and small shapes
+    cases = [(512, 28672, 74), (512, 3584, 74), (512, 7168, 74), (512, 14336, 74),
+             (512, 9728, 74), (500, 9728, 74), (300, 1024, 74), (9, 256, 74), (8192, 28672, 74)]
+    cases += [(rng.randint(9, 3000), rng.randint(1, 150) * 128, rng.randint(1, 74))
+              for _ in range(400)]
+    hit = {}
+    for rows, np_, maxp in cases:
+        tok, ntt, tiles, sk_tiles, split = _plan_tok(rows, np_, maxp)
+        if (rows, np_, maxp) == (512, 28672, 74):
+            assert (tok, tiles, sk_tiles, split) == (256, 224, 2, 8)
+        if (rows, np_, maxp) == (512, 3584, 74):
+            assert (tok, tiles, sk_tiles, split) == (128, 56, 0, 1)
+        P = min(tiles, maxp)
+        assert (tiles - sk_tiles) % P == 0 or sk_tiles == 0
+        cover = np.zeros(((np_ + 255) // 256, ntt * tok), np.int32)
+        for cid in range(P):
+            for t in _tail_items(tiles, sk_tiles, split, P, cid):
+                tc, tok0, ntok = _tile_geom(t, tiles, ntt, tok, sk_tiles, split)
+                assert ntok >= 32 and ntok % 32 == 0 and ntok <= tok
+                cover[tc, tok0:tok0 + ntok] += 1
+        assert (cover == 1).all(), (rows, np_, maxp)
+        hit[split > 1] = True
+    assert hit.get(True) and hit.get(False)
