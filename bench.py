@@ -314,27 +314,36 @@ def run_ours(args, rank, world, local_rank):
         if i % 64 == 63:
             torch.cuda.synchronize(dev)
     torch.cuda.synchronize(dev)
-    backend.profile(True)
     barrier()
     torch.cuda.synchronize(dev)
+
+    def timed_steps():
+        # Hold the GPU while the host enqueues every timed step, so the events measure
+        # device time only (no host launch gaps inside a step).
+        times = []
+        torch.cuda._sleep(int(2e8))
+        for _ in range(args.steps):
+            flush.zero_()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            step()
+            e1.record()
+            times.append((e0, e1))
+        torch.cuda.synchronize(dev)
+        barrier()
+        return times
+
+    # The timed region: the steps as a caller runs them (no per-kernel events inside).
     launches_before = backend.launches()
-    times = []
-    # Hold the GPU while the host enqueues every timed step, so the events measure device
-    # time only (no host launch gaps inside a step).
-    torch.cuda._sleep(int(2e8))
-    for _ in range(args.steps):
-        flush.zero_()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        step()
-        e1.record()
-        times.append((e0, e1))
-    torch.cuda.synchronize(dev)
-    barrier()
+    times = timed_steps()
     launches_timed = backend.launches() - launches_before
     clocks = sampler.stop()
     clocks["window"] = f"{soak_steps}-step untimed soak of the same step + the timed region"
+    # The per-kernel breakdown (GEMM, act-quant) from the same number of steps run again with
+    # the library's per-kernel events on; not part of `value`.
+    backend.profile(True)
+    timed_steps()
     backend.profile(False)
     quant_ms, main_ms, calls = backend.profile_collect()
     backend.check(stream)
