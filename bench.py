@@ -70,6 +70,15 @@ def parse():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
+    ap.add_argument("--sweep", action="store_true",
+                    help="one GPU: one JSON line per named shape (cfg0-cfg4 and their M sweeps) "
+                         "instead of the headline line")
+    ap.add_argument("--sweep-cases", default="",
+                    help="comma-separated case-name prefixes to run with --sweep (default all)")
+    ap.add_argument("--swiglu-unfused", action="store_true",
+                    help="prefill SwiGLU as GEMM -> f32 workspace -> SwiGLU pass (comparison)")
+    ap.add_argument("--stream-k", action="store_true",
+                    help="let the GEMM choose its stream-K schedule (QLINEAR_BACKEND_GEMM_STREAM_K)")
     return ap.parse_args()
 
 
@@ -543,6 +552,191 @@ def e2e_measure(backend, lin, torch, dist, dev, args, world, m, k, n, ns, x_host
                    "qlinear_interleave_columns -> D2H f32"}
 
 
+def run_sweep(args):
+    """--sweep: every named shape on one GPU, one JSON line each.
+
+    Every case runs its calls back to back (the way a model runs its linears) over enough
+    distinct weight copies that each call streams its weights from HBM (a rotation larger
+    than the L2 cache, or one layer set larger than it); activations are re-used and may sit
+    in L2.  Time = CUDA events around a whole rotation, the GPU held by a sleep kernel while
+    the host enqueues, median of 5.  TOPS = 2*M*K*N (summed over the case's linears) / time;
+    GB/s = the case's algorithmic bytes (weights as stored for the kernel that reads them,
+    scales, fp16 activations in and out) / time.
+    """
+    import torch
+    from open_rknpu2_lm_infer_b200 import Backend, QuantMatrix
+    from open_rknpu2_lm_infer_b200 import workloads as W
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    backend = Backend(device=0, swiglu_unfused=args.swiglu_unfused, gemm_stream_k=args.stream_k)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    hbm = measured_peaks().get("hbm_gbs", 6650.0)
+    int8_peak = int8_peak_tops(torch, dev)
+    only = [s for s in args.sweep_cases.split(",") if s]
+    codes_cache = {}
+
+    def load(bits, k, n, copies):
+        key = (bits, k, n)
+        if key not in codes_cache:
+            codes_cache[key] = (W.weight_codes(bits, k, n), W.weight_scales(n))
+        c, s = codes_cache[key]
+        return [backend.load(QuantMatrix(bits, k, n, c, s)) for _ in range(copies)]
+
+    def act(m, k, stream_id=0):
+        return torch.from_numpy(W.activations(m, k, stream=stream_id)).to(dev)
+
+    def time_chain(chain, reps=5):
+        """chain(): enqueue one rotation; returns seconds per rotation (median)."""
+        chain()
+        chain()
+        torch.cuda.synchronize(dev)
+        runs = []
+        for _ in range(reps):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            torch.cuda._sleep(int(5e7))
+            e0.record()
+            chain()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            runs.append(e0.elapsed_time(e1) * 1e-3)
+        backend.check(stream)
+        return statistics.median(runs)
+
+    def copies_for(bytes_per_copy):
+        return max(2, min(16, -(-4 * l2 // max(1, bytes_per_copy))))
+
+    def kernel_bytes(bits, k, n, m):
+        """Weight bytes the path's kernel reads: the packed W4 copy for the decode GEMV
+        (M <= 8), the int8 copy otherwise (W4 prefill reads its int8 expansion)."""
+        wb = k * n * (bits // 8 if bits == 8 else (1 if m > 8 else 0.5))
+        return int(wb) + 4 * n
+
+    def emit(case, m, secs, ops, bytes_, launches, extra=None):
+        line = {"sweep": case, "M": m, "us": secs * 1e6, "tops": ops / secs / 1e12,
+                "gbs": bytes_ / secs / 1e9,
+                "frac_int8_peak": ops / secs / 1e12 / int8_peak,
+                "frac_hbm": bytes_ / secs / 1e9 / hbm,
+                "bound": "hbm" if m <= 16 else "tensor",
+                "launches": launches}
+        if extra:
+            line.update(extra)
+        print(json.dumps(line), flush=True)
+
+    def want(name):
+        return not only or any(name.startswith(p) for p in only)
+
+    sampler = ClockSampler(0)
+    sampler.start()
+    launches0 = backend.launches()
+
+    # single linears: cfg0 (W4A8 M512), cfg1 (W8A8 M1, M4), cfg4 (W4A8 M 1/8/512/8192)
+    singles = [("cfg0", 4, 2560, 9728, (512,)), ("cfg1", 8, 2560, 9728, (1, 4)),
+               ("cfg4", 4, 8192, 28672, (1, 8, 512, 8192))]
+    for name, bits, k, n, ms in singles:
+        if not want(name):
+            continue
+        ncopy = copies_for(kernel_bytes(bits, k, n, max(ms)))
+        lins = load(bits, k, n, ncopy)
+        for m in ms:
+            x = act(m, k)
+            y = torch.empty((m, n), dtype=torch.float16, device=dev)
+            reps = max(1, min(8, int(2e11 / (2.0 * m * k * n * ncopy)) + 1))
+
+            def chain():
+                for _ in range(reps):
+                    for lin in lins:
+                        lin.run_device(x, y, m, stream=stream)
+            b0 = backend.launches()
+            secs = time_chain(chain) / (reps * ncopy)
+            launches = (backend.launches() - b0) / (7 * reps * ncopy)
+            emit(f"{name} W{bits}A8 K{k} N{n}", m, secs, 2.0 * m * k * n,
+                 kernel_bytes(bits, k, n, m) + 2 * m * k + 2 * m * n, launches,
+                 {"copies": ncopy})
+            del x, y
+        for lin in lins:
+            lin.close()
+        del lins
+        codes_cache.clear()
+
+    # cfg2: MLP block gate/up W4 (2560 -> 2x9728, SwiGLU in the epilogue) -> down W8
+    if want("cfg2"):
+        k, h = 2560, 9728
+        blk_bytes = kernel_bytes(4, k, 2 * h, 512) + kernel_bytes(8, h, k, 512)
+        ncopy = copies_for(blk_bytes)
+        gus = load(4, k, 2 * h, ncopy)
+        downs = load(8, h, k, ncopy)
+        for m in (1, 16, 128, 512, 4096):
+            x = act(m, k)
+            mid = torch.empty((m, h), dtype=torch.float16, device=dev)
+            y = torch.empty((m, k), dtype=torch.float16, device=dev)
+
+            def chain():
+                for gu, dn in zip(gus, downs):
+                    gu.run_device(x, mid, m, swiglu=True, stream=stream)
+                    dn.run_device(mid, y, m, stream=stream)
+            b0 = backend.launches()
+            secs = time_chain(chain) / ncopy
+            launches = (backend.launches() - b0) / (7 * ncopy)
+            ops = 2.0 * m * k * 2 * h + 2.0 * m * h * k
+            bytes_ = (kernel_bytes(4, k, 2 * h, m) + kernel_bytes(8, h, k, m)
+                      + 2 * m * k + 2 * m * h + 2 * m * h + 2 * m * k)
+            emit("cfg2 MLP block W4 gate/up+SwiGLU -> W8 down", m, secs, ops, bytes_, launches,
+                 {"copies": ncopy})
+        for lin in gus + downs:
+            lin.close()
+        del gus, downs
+        codes_cache.clear()
+
+    # cfg3: the linears of 36 decoder layers (W4/W8 per linear from the seeded draw)
+    if want("cfg3"):
+        draw = W.layer_bits()
+        layers = []
+        for li, row in enumerate(draw):
+            layer = []
+            for (lname, k, n), bits in zip(W.QWEN3_4B_LAYER, row):
+                layer.append((lname, bits, k, n, load(bits, k, n, 1)[0]))
+            layers.append(layer)
+        n_w4 = sum(b == 4 for row in draw for b in row)
+        for m in (1, 512):
+            xs = {k: act(m, k, stream_id=k) for k in (2560, 4096)}
+            outs = {n: torch.empty((m, n), dtype=torch.float16, device=dev)
+                    for n in (6144, 2560, 9728)}
+
+            def chain():
+                for layer in layers:
+                    for lname, bits, k, n, lin in layer:
+                        if lname == "gate_up":
+                            lin.run_device(xs[2560], outs[9728], m, swiglu=True, stream=stream)
+                        elif lname == "down":
+                            lin.run_device(outs[9728], outs[2560], m, stream=stream)
+                        else:
+                            lin.run_device(xs[k], outs[n], m, stream=stream)
+            b0 = backend.launches()
+            secs = time_chain(chain, reps=3)
+            launches = (backend.launches() - b0) / 5
+            ops = sum(2.0 * m * k * n for layer in layers for _, _, k, n, _ in layer)
+            bytes_ = sum(kernel_bytes(bits, k, n, m) + 2 * m * k
+                         + 2 * m * (n // 2 if lname == "gate_up" else n)
+                         for layer in layers for lname, bits, k, n, _ in layer)
+            emit(f"cfg3 36 layers x (qkv, o, gate/up+SwiGLU, down), {n_w4}/144 linears W4",
+                 m, secs, ops, bytes_, launches, {"ms_per_pass": secs * 1e3})
+        for layer in layers:
+            for *_, lin in layer:
+                lin.close()
+
+    clocks = sampler.stop()
+    print(json.dumps({"sweep_done": True, "swiglu": "unfused" if args.swiglu_unfused else
+                      "fused in the GEMM epilogue (prefill)", "stream_k": args.stream_k,
+                      "int8_peak_tops": int8_peak,
+                      "hbm_gbs": hbm,
+                      "l2_bytes": l2, "clocks": clocks,
+                      "launches_total": backend.launches() - launches0}), flush=True)
+    backend.close()
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -552,6 +746,10 @@ def main():
         print(f"--gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.sweep:
+        if world == 1:
+            run_sweep(args)
         return
     if world > 1:
         import datetime

@@ -82,6 +82,11 @@ typedef struct qlinear_weights qlinear_weights;
  * that finishes split tiles is bound by the epilogue's output stores and loses to the
  * whole-tile schedule on every shape measured so far. */
 #define QLINEAR_BACKEND_GEMM_STREAM_K 2u
+/* Run the prefill SwiGLU (QLINEAR_RUN_SWIGLU above the decode row count) as the GEMM into
+ * an f32 [rows][N] workspace followed by a separate SiLU-gated-product pass, instead of the
+ * GEMM whose epilogue computes the product (the default for weights with an 8-bit prefill
+ * copy).  Both give bit-identical results; this is for comparison and testing. */
+#define QLINEAR_BACKEND_SWIGLU_UNFUSED 4u
 
 typedef struct qlinear_backend_config {
     int device;     /* CUDA device ordinal (replaces the IOMMU domain id, src/npu.rs:310) */

@@ -37,6 +37,7 @@ class QLinearUnavailable(RuntimeError):
 
 BACKEND_W4_PACKED_ONLY = 1
 BACKEND_GEMM_STREAM_K = 2
+BACKEND_SWIGLU_UNFUSED = 4
 IPC_HANDLE_BYTES = 64
 
 

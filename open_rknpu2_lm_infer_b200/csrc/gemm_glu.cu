@@ -1,0 +1,27 @@
+// gemm_glu.cu -- prefill path for Linear::run_swiglu (src/npu.rs:1009-1024): the tcgen05
+// GEMM of a gate/up matrix with the SiLU-gated product in its epilogue, so the [rows][N]
+// projection output is never written.  The kernel is gemm_kernel<8, OutT, 1, true> in
+// gemm_impl.cuh.
+#include "gemm_impl.cuh"
+
+namespace ql {
+
+cudaError_t launch_gemm_glu(const WeightView &w, const CUtensorMap &wmap_glu, const ActView &a,
+                            const CUtensorMap &amap, const CUtensorMap &amap_sub,
+                            const GemmPlan &plan, int rows, void *out, int out_type,
+                            long long ldc, unsigned *err, bool pdl, cudaStream_t stream) {
+    // whole tiles only (the epilogue has no stream-K partial-sum path), 8-bit weights, an
+    // even N, a floating-point output
+    if (plan.sk == 1 || w.bits != 8 || w.N % 2 != 0 || !out || ldc < w.N / 2)
+        return cudaErrorInvalidValue;
+    GemmArgs args = make_args(w, a, plan, rows, ldc, err, nullptr);
+    args.out = out;
+    const OutputSet none{};
+    if (out_type == kF16)
+        return launch_s<8, __half, 1, true>(wmap_glu, amap, amap_sub, args, none, plan, pdl, stream);
+    if (out_type == kF32)
+        return launch_s<8, float, 1, true>(wmap_glu, amap, amap_sub, args, none, plan, pdl, stream);
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace ql

@@ -236,7 +236,17 @@ __device__ __forceinline__ uint64_t smem_desc_sw128_k(const void *tile) {
 // separate trailing parameter, not a GemmArgs field: growing GemmArgs changed the register
 // allocation of the single-output kernel (168 -> 150 registers) and measured 2.2x slower on
 // B200.
-template <int BITS, typename OutT, int NDST>
+//
+// GLU (8-bit weights, one output): the SiLU-gated product of a gate/up matrix (gate columns
+// [0, N/2), up columns [N/2, N), the order src/model/checkpoint.rs:392-423 concatenates
+// them) in the epilogue.  Channel tile tc covers the 128 output channels [128 tc, 128 tc +
+// 128): CTA `rank` stages, per 32-row quadrant q of its weight slot, 16 gate rows
+// c0 .. c0 + 15 and then the 16 up rows N/2 + c0 .. with c0 = 128 tc + 64 rank + 16 q (two
+// boxes of 16 rows through `wmap`, whose box is 16 rows high).  So lane l < 16 of the
+// epilogue warp of quadrant q holds gate channel c0 + l and lane l + 16 its up channel: one
+// shuffle per token pair hands each lane the other half, and each lane stores
+// silu(g) * u (src/npu.rs:1202-1208) for every other token.  No [M][N] intermediate.
+template <int BITS, typename OutT, int NDST, bool GLU = false>
 __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap amap,
                 const GemmArgs p, const OutputSet outs,
@@ -306,9 +316,18 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
         if (lane == 0) {
             // tx: the bytes the leader's `full` barrier receives for the stage from both CTAs
             auto load_weights = [&](int s, int kb, int tc, uint32_t tx) {
-                if (BITS == 8)
+                if constexpr (GLU) {
+                    // quadrant q: gate rows c0 .. c0 + 15, then up rows N/2 + c0 ..
+#pragma unroll
+                    for (int b = 0; b < 8; b++)
+                        tma_load_2d_pair(sW + s * w_slot + b * 16 * KB, &wmap, full0 + 8u * s,
+                                         kb * KB,
+                                         (b & 1) * (p.N / 2) + tc * CH_CTA + (int)rank * 64 +
+                                             (b >> 1) * 16);
+                } else if (BITS == 8) {
                     tma_load_2d_pair(sW + s * w_slot, &wmap, full0 + 8u * s, kb * KB,
                                      tc * CHT + (int)rank * CH_CTA);
+                }
                 if (rank == 0) mbar_arrive_expect_tx(&full[s], tx);
             };
             // Weight tiles of the first stages do not depend on the preceding kernel:
@@ -396,7 +415,8 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
         const int q = warp & 3;                 // TMEM lane quadrant this warp may access
         const int colh = (warp - 2) >> 2;       // which half of the tok columns
         const int sub = (int)rank * EPI_WARPS + (warp - 2);  // this warp's part of a tile
-        const int chl = (int)rank * CH_CTA + q * 32 + lane;  // channel within the tile
+        const int chl = GLU ? (int)rank * 64 + q * 16 + (lane & 15)  // output channel
+                            : (int)rank * CH_CTA + q * 32 + lane;  // channel within the tile
         uint32_t local = 0;
         // Activation scales (and W4 row sums) of this warp's columns, loaded once per tile:
         // column c of the warp's range sits in lane c % 32 of register c / 32.
@@ -453,6 +473,35 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                 }
             }
         };
+        // GLU: dequantise chunk cc, swap halves with the partner lane (l ^ 16), and store
+        // silu(g) * u: gate lanes the chunk's even tokens, up lanes the odd ones.
+        auto emit16_glu = [&](const uint32_t (&r)[16], int cc, int tok_base, int ch, bool chv,
+                              float sw) {
+            const bool up = lane >= 16;
+            float y[16];
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const int src = (cc & 1) * 16 + j;
+                const float sa = __shfl_sync(0xffffffffu, sa_r[cc >> 1], src);
+                const int rs = __shfl_sync(0xffffffffu, rs_r[cc >> 1], src);
+                int acc = (int)r[j];
+                if (BITS == 4) acc -= 8 * rs;
+                y[j] = __fmul_rn(__fmul_rn(__int2float_rn(acc), sa), sw);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const float other = __shfl_xor_sync(0xffffffffu, up ? y[2 * i] : y[2 * i + 1], 16);
+                const float g = up ? other : y[2 * i];
+                const float u = up ? y[2 * i + 1] : other;
+                const int m = tok_base + cc * 16 + 2 * i + (up ? 1 : 0);
+                if constexpr (!std::is_same<OutT, int32_t>::value) {
+                    if (chv && m < p.M) {
+                        const float v = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+                        out[(long long)m * p.ldc + ch] = OutCvt<OutT>::from(v);
+                    }
+                }
+            }
+        };
         const int pg = p.sk == 1 ? (int)ncl / p.n_tok_tiles : 1;  // stream-K pairs per group
         Sched se(p, (int)cid, (int)ncl);
         int t, kb0, kb1;
@@ -466,14 +515,15 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
             const bool okw = mbar_wait(&accf[ab], (local >> 1) & 1, err, abort_flag);
             if (!__all_sync(0xffffffffu, okw)) break;
             tc_fence_after();
-            const int ch = tc * CHT + chl;
-            const bool chv = ch < p.N;
+            const int ch = GLU ? tc * CH_CTA + chl : tc * CHT + chl;
+            const bool chv = ch < (GLU ? p.N / 2 : p.N);
             const int tok_base = tok0 + colh * cols;
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) +
                                    (uint32_t)(ab * tok + colh * cols);
             if (kb0 == 0 && kb1 == p.nkb) {
                 // the whole tile: dequantise from tensor memory
-                const float sw = chv ? p.wscale[ch] : 0.0f;
+                const float sw =
+                    chv ? p.wscale[(GLU && lane >= 16 ? p.N / 2 : 0) + ch] : 0.0f;
                 load_scales(tok_base, cols);
 #pragma unroll
                 for (int cc = 0; cc < 8; cc++) {
@@ -481,13 +531,17 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                     uint32_t r[16];
                     tmem_ld16(taddr + cc * 16, r);
                     tmem_ld_wait();
-                    emit16(r, cc, tok_base, ch, chv, sw);
+                    if constexpr (GLU)
+                        emit16_glu(r, cc, tok_base, ch, chv, sw);
+                    else
+                        emit16(r, cc, tok_base, ch, chv, sw);
                 }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive_remote(acce0 + 8u * ab);
                 continue;
             }
+            if constexpr (GLU) break;  // GLU plans have whole tiles only (no stream-K)
             // A segment of a split tile.  Its partial sums go to its own workspace buffer
             // ([tok][256] int32, lanes = consecutive channels): the tile's first segment
             // (it ends at the tile's first boundary b_f) to "left" of b_f, every other one
@@ -653,12 +707,12 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
     }
 }
 
-template <int BITS, typename OutT, int NDST>
+template <int BITS, typename OutT, int NDST, bool GLU = false>
 cudaError_t launch_s(const CUtensorMap &wmap, const CUtensorMap &amap,
                      const CUtensorMap &amap_sub, const GemmArgs &args,
                      const OutputSet &outs, const GemmPlan &plan, bool pdl,
                      cudaStream_t stream) {
-    auto kern = gemm_kernel<BITS, OutT, NDST>;
+    auto kern = gemm_kernel<BITS, OutT, NDST, GLU>;
     // The opt-in shared-memory limit is a per-device, per-kernel attribute: set it once per
     // device (an attribute call per launch costs host time).
     static int configured[64] = {0};

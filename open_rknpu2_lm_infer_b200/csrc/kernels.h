@@ -115,6 +115,14 @@ cudaError_t launch_gemm(const WeightView &w, const CUtensorMap &wmap, const ActV
                         const OutputSet &out,
                         int out_type, long long ldc, unsigned *err, void *sk_ws, bool pdl,
                         cudaStream_t stream);
+// SwiGLU in the GEMM's epilogue (gemm_glu.cu): w is an 8-bit gate/up matrix (N even, gate
+// columns first), wmap_glu its map from encode_glu_map (16-row boxes), plan from plan_gemm
+// without stream-K; out [rows][ldc] (ldc >= N/2) of kF16 or kF32 receives
+// silu(y[m][j]) * y[m][N/2 + j].
+cudaError_t launch_gemm_glu(const WeightView &w, const CUtensorMap &wmap_glu, const ActView &a,
+                            const CUtensorMap &amap, const CUtensorMap &amap_sub,
+                            const GemmPlan &plan, int rows, void *out, int out_type,
+                            long long ldc, unsigned *err, bool pdl, cudaStream_t stream);
 // The same with out.count > 1 (launch_gemm forwards to it): the split-N exchange's GEMM.
 cudaError_t launch_gemm_scatter(const WeightView &w, const CUtensorMap &wmap, const ActView &a,
                                 const CUtensorMap &amap, const CUtensorMap &amap_sub,
@@ -153,6 +161,8 @@ bool weights_for_noalloc(const qlinear_weights *w, WeightView *view, int *device
 // TMA descriptor encoding through the driver entry point (no -lcuda link needed).
 bool tma_available();
 bool encode_weight_map(const WeightView &w, CUtensorMap *map);
+// 8-bit weights [Np][Kp] in boxes of 128 k x 16 channels (the SwiGLU GEMM's gate/up boxes).
+bool encode_glu_map(const WeightView &w, CUtensorMap *map);
 bool encode_act_map(const int8_t *codes, int rows_cap, int Kp, int tok, CUtensorMap *map);
 
 }  // namespace ql

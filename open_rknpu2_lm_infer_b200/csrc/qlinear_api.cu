@@ -66,7 +66,8 @@ struct qlinear_backend {
     int max_kp = 0, max_n = 0;
     int prepared_rows = 0;
     unsigned long long launches = 0;
-    unsigned long long gemv_calls = 0, gemm_calls = 0, gemm_stream_k_calls = 0;
+    unsigned long long gemv_calls = 0, gemm_calls = 0, gemm_stream_k_calls = 0,
+                       gemm_glu_calls = 0;
     std::map<std::tuple<const void *, int, int, size_t>, CUtensorMap> amaps;
     // per-kernel device timing (qlinear_backend_profile)
     bool profiling = false;
@@ -86,6 +87,10 @@ struct qlinear_weights {
     WeightView view8{};
     uint8_t *d_w8 = nullptr;
     CUtensorMap wmap8{};
+    // even N with an 8-bit prefill copy: that copy in 16-channel boxes for the GEMM with
+    // the SwiGLU epilogue (gate and up rows of a channel staged side by side)
+    bool has_glu = false;
+    CUtensorMap wmap_glu{};
 };
 
 namespace {
@@ -169,6 +174,10 @@ bool encode_weight_map(const WeightView &w, CUtensorMap *map) {
         return encode_2d(map, w.w, w.Kp, w.Np, w.Kp, GEMM_KB, CH_TILE, CU_TENSOR_MAP_SWIZZLE_128B);
     return encode_2d(map, w.w, w.Kp / 2, w.Np, w.Kp / 2, GEMM_KB / 2, CH_TILE,
                      CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+bool encode_glu_map(const WeightView &w, CUtensorMap *map) {
+    if (w.bits != 8) return false;
+    return encode_2d(map, w.w, w.Kp, w.Np, w.Kp, GEMM_KB, 16, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 bool encode_act_map(const int8_t *codes, int rows_cap, int Kp, int tok, CUtensorMap *map) {
     return encode_2d(map, codes, Kp, rows_cap, Kp, GEMM_KB, tok / 2, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -343,7 +352,11 @@ int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_
     const bool use8 = w->d_w8 != nullptr;
     const WeightView &gv = use8 ? w->view8 : v;
     const CUtensorMap &gmap = use8 ? w->wmap8 : w->wmap;
-    const GemmPlan plan = plan_gemm(gv, rows, pairs, (b->flags & QLINEAR_BACKEND_GEMM_STREAM_K) != 0);
+    // SwiGLU in the GEMM's epilogue: one output buffer, 8-bit prefill weights
+    const bool glu = swiglu && w->has_glu && outs.count == 1 &&
+                     !(b->flags & QLINEAR_BACKEND_SWIGLU_UNFUSED);
+    const GemmPlan plan =
+        plan_gemm(gv, rows, pairs, !glu && (b->flags & QLINEAR_BACKEND_GEMM_STREAM_K) != 0);
     if ((st = ensure_sk(b, gemm_sk_bytes(plan)))) return st;
     if (plan.sk == 1) b->gemm_stream_k_calls++;
     const CUtensorMap *amap = nullptr;
@@ -359,6 +372,11 @@ int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_
         QL_TRY(launch_gemm(gv, gmap, av, *amap, *amap_sub, plan, rows, outs, c_type, ldc,
                            b->d_err, b->d_sk, true, stream));
         b->launches++;
+    } else if (glu) {
+        QL_TRY(launch_gemm_glu(gv, w->wmap_glu, av, *amap, *amap_sub, plan, rows, c_dev, c_type,
+                               ldc, b->d_err, true, stream));
+        b->launches++;
+        b->gemm_glu_calls++;
     } else {
         st = ensure_dev(reinterpret_cast<void **>(&b->d_y), &b->y_elems,
                         (size_t)rows * v.N * sizeof(float));
@@ -444,6 +462,11 @@ qlinear_weights *weights_create_common(qlinear_backend *b, const qlinear_weight_
         if (!encode_weight_map(w->view8, &w->wmap8)) return cleanup(QLINEAR_ERR_CUDA);
         w->bytes += bytes8;
     }
+    if (N % 2 == 0 && (v.bits == 8 || w->d_w8)) {
+        if (!encode_glu_map(v.bits == 8 ? v : w->view8, &w->wmap_glu))
+            return cleanup(QLINEAR_ERR_CUDA);
+        w->has_glu = true;
+    }
     b->weight_bytes += w->bytes;
     (v.bits == 4 ? b->loaded_w4 : b->loaded_w8)++;
     b->max_kp = std::max(b->max_kp, v.Kp);
@@ -484,7 +507,8 @@ qlinear_backend *qlinear_backend_create(const qlinear_backend_config *cfg) {
     if (cfg->round_mode != QLINEAR_ROUND_AWAY && cfg->round_mode != QLINEAR_ROUND_EVEN)
         return fail(QLINEAR_ERR_PARAM), nullptr;
     if (cfg->max_rows < 0 ||
-        (cfg->flags & ~(QLINEAR_BACKEND_W4_PACKED_ONLY | QLINEAR_BACKEND_GEMM_STREAM_K)))
+        (cfg->flags & ~(QLINEAR_BACKEND_W4_PACKED_ONLY | QLINEAR_BACKEND_GEMM_STREAM_K |
+                        QLINEAR_BACKEND_SWIGLU_UNFUSED)))
         return fail(QLINEAR_ERR_PARAM), nullptr;
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || cfg->device < 0 || cfg->device >= ndev)
@@ -857,13 +881,14 @@ int qlinear_backend_stats(const qlinear_backend *b, char *buf, size_t len) {
         "\"tune_cache_misses\": 0, \"tune_calls\": 0, \"strategy_fallbacks\": 0, "
         "\"strategy_fallback_calls\": 0, \"weight_reload_calls\": 0, \"round_mode\": \"%s\", "
         "\"prepared_rows\": %d, \"kernel_launches\": %llu, \"gemv_calls\": %llu, "
-        "\"gemm_calls\": %llu, \"gemm_stream_k_calls\": %llu, "
+        "\"gemm_calls\": %llu, \"gemm_stream_k_calls\": %llu, \"gemm_swiglu_fused_calls\": %llu, "
         "\"gemm_pairs_resident\": [%d, %d]}",
         b->device, b->num_sms, b->loaded_w4, b->loaded_w8, (unsigned long long)b->weight_bytes,
         (unsigned long long)ws, b->ws_bytes ? 1 : 0,
         (unsigned long long)(b->h_in_bytes + b->h_out_bytes),
         b->round_mode == QLINEAR_ROUND_AWAY ? "away" : "even", b->prepared_rows, b->launches,
-        b->gemv_calls, b->gemm_calls, b->gemm_stream_k_calls, b->gemm_pairs[0], b->gemm_pairs[1]);
+        b->gemv_calls, b->gemm_calls, b->gemm_stream_k_calls, b->gemm_glu_calls, b->gemm_pairs[0],
+        b->gemm_pairs[1]);
     if (n < 0) return QLINEAR_ERR_PARAM;
     if (buf && len) {
         std::strncpy(buf, tmp, len - 1);

@@ -78,13 +78,15 @@ class Backend:
     (src/npu.rs:230-254).  Single-threaded, like the reference's Rc<RefCell<..>>."""
 
     def __init__(self, device: int = 0, round_mode: int = L.ROUND_AWAY, max_rows: int = 256,
-                 w4_packed_only: bool = False, gemm_stream_k: bool = False):
+                 w4_packed_only: bool = False, gemm_stream_k: bool = False,
+                 swiglu_unfused: bool = False):
         self._lib = L.load()
         cfg = L.BackendConfig()
         self._lib.qlinear_backend_config_init(ctypes.byref(cfg))
         cfg.device, cfg.round_mode, cfg.max_rows = device, round_mode, max_rows
         cfg.flags = ((L.BACKEND_W4_PACKED_ONLY if w4_packed_only else 0) |
-                     (L.BACKEND_GEMM_STREAM_K if gemm_stream_k else 0))
+                     (L.BACKEND_GEMM_STREAM_K if gemm_stream_k else 0) |
+                     (L.BACKEND_SWIGLU_UNFUSED if swiglu_unfused else 0))
         raw = self._lib.qlinear_backend_create(ctypes.byref(cfg))
         if not raw:
             raise NpuError("create CUDA backend", self._lib.qlinear_last_status())
