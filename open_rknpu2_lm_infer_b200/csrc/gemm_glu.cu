@@ -9,12 +9,13 @@ namespace ql {
 cudaError_t launch_gemm_glu(const WeightView &w, const CUtensorMap &wmap_glu, const ActView &a,
                             const CUtensorMap &amap, const CUtensorMap &amap_sub,
                             const GemmPlan &plan, int rows, void *out, int out_type,
-                            long long ldc, unsigned *err, bool pdl, cudaStream_t stream) {
-    // whole tiles only (the epilogue has no stream-K partial-sum path), 8-bit weights, an
-    // even N, a floating-point output
-    if (plan.sk == 1 || w.bits != 8 || w.N % 2 != 0 || !out || ldc < w.N / 2)
+                            long long ldc, unsigned *err, void *sk_ws, bool pdl,
+                            cudaStream_t stream) {
+    // 8-bit weights, an even N, a floating-point output; sk_ws: the stream-K workspace of
+    // gemm_sk_bytes(plan) bytes when the plan chose stream-K
+    if (w.bits != 8 || w.N % 2 != 0 || !out || ldc < w.N / 2 || (plan.sk == 1 && !sk_ws))
         return cudaErrorInvalidValue;
-    GemmArgs args = make_args(w, a, plan, rows, ldc, err, nullptr);
+    GemmArgs args = make_args(w, a, plan, rows, ldc, err, sk_ws);
     args.out = out;
     const OutputSet none{};
     if (out_type == kF16)

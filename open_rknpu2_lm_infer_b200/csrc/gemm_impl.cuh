@@ -415,8 +415,9 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
         const int q = warp & 3;                 // TMEM lane quadrant this warp may access
         const int colh = (warp - 2) >> 2;       // which half of the tok columns
         const int sub = (int)rank * EPI_WARPS + (warp - 2);  // this warp's part of a tile
+        const int tl = (int)rank * CH_CTA + q * 32 + lane;  // tensor-memory lane in the tile
         const int chl = GLU ? (int)rank * 64 + q * 16 + (lane & 15)  // output channel
-                            : (int)rank * CH_CTA + q * 32 + lane;  // channel within the tile
+                            : tl;                                    // channel within the tile
         uint32_t local = 0;
         // Activation scales (and W4 row sums) of this warp's columns, loaded once per tile:
         // column c of the warp's range sits in lane c % 32 of register c / 32.
@@ -541,7 +542,6 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                 if (lane == 0) mbar_arrive_remote(acce0 + 8u * ab);
                 continue;
             }
-            if constexpr (GLU) break;  // GLU plans have whole tiles only (no stream-K)
             // A segment of a split tile.  Its partial sums go to its own workspace buffer
             // ([tok][256] int32, lanes = consecutive channels): the tile's first segment
             // (it ends at the tile's first boundary b_f) to "left" of b_f, every other one
@@ -565,7 +565,7 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                 const int col0 = colh * cols + cc * 16;
 #pragma unroll
                 for (int j = 0; j < 16; j++)
-                    st_l2_hint(mine + (long long)(col0 + j) * CHT + chl, (int)r[j], keep);
+                    st_l2_hint(mine + (long long)(col0 + j) * CHT + tl, (int)r[j], keep);
             }
             tc_fence_before();
             __syncwarp();
@@ -577,7 +577,8 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
             last = __shfl_sync(0xffffffffu, last, 0);
             if (!last) continue;
             __threadfence();
-            const float sw = chv ? p.wscale[ch] : 0.0f;
+            const float sw =
+                chv ? p.wscale[(GLU && lane >= 16 ? p.N / 2 : 0) + ch] : 0.0f;
             load_scales(tok_base, cols);
             // the tile's buffers: left of b_f, right of b_f .. b_f + nseg - 2.  Two chunks at
             // a time, the loads of both first buffers issued together: under the main loops'
@@ -596,7 +597,7 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                 for (int h = 0; h < 2; h++)
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
-                        const long long off = (long long)(col0 + h * 16 + j) * CHT + chl;
+                        const long long off = (long long)(col0 + h * 16 + j) * CHT + tl;
                         r[h][j] = (h == 0 || two) ? (uint32_t)ld_l2_hint(left + off, drop) : 0u;
                         q2[h][j] = (h == 0 || two) ? (uint32_t)ld_l2_hint(right0 + off, drop) : 0u;
                     }
@@ -612,10 +613,15 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                         for (int j = 0; j < 16; j++)
                             if (h == 0 || two)
                                 r[h][j] += (uint32_t)ld_l2_hint(
-                                    right + (long long)(col0 + h * 16 + j) * CHT + chl, drop);
+                                    right + (long long)(col0 + h * 16 + j) * CHT + tl, drop);
                 }
-                emit16(r[0], cc, tok_base, ch, chv, sw);
-                if (two) emit16(r[1], cc + 1, tok_base, ch, chv, sw);
+                if constexpr (GLU) {
+                    emit16_glu(r[0], cc, tok_base, ch, chv, sw);
+                    if (two) emit16_glu(r[1], cc + 1, tok_base, ch, chv, sw);
+                } else {
+                    emit16(r[0], cc, tok_base, ch, chv, sw);
+                    if (two) emit16(r[1], cc + 1, tok_base, ch, chv, sw);
+                }
             }
             if (lane == 0) p.sk_cnt[slot * (2 * EPI_WARPS) + sub] = 0;
         }

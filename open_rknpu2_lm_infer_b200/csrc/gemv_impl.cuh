@@ -45,7 +45,15 @@ constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
 constexpr int kSmemBudget = 220 * 1024;
 constexpr int kMaxUnits = 16;        // units per lane per task (longer rows are split in chunks)
-constexpr int kMaxUnitsSwiglu = 8;   // swiglu tasks carry two rows
+constexpr int kMaxUnitsSwiglu = 8;   // swiglu and paired tasks carry two rows
+
+// Tasks of two weight rows where the activation reads from shared memory would otherwise
+// bound the kernel: per weight byte and activation row, W4 reads two bytes of codes and W8
+// one, and an SM reads 128 bytes of shared memory per clock.  A task of two rows (the first
+// and second half of the CTA's rows) reads each activation chunk once for both.
+__host__ __device__ constexpr bool gemv_paired(int bits, int mt, bool swiglu) {
+    return !swiglu && (bits == 4 ? mt >= 4 : mt >= 8);
+}
 
 // Register ring depth for NSEG*U units per lane per task: about 96 data registers per thread
 // with one or two activation rows, less with more (their partial sums need registers too).
@@ -98,6 +106,31 @@ __device__ __forceinline__ void store_all(const OutputSet &o, int type, long lon
         if (d < o.count) store_typed(o.dst[d], type, idx + o.col0, y, raw);
 }
 
+// Where code k of an activation row sits in shared memory.  W8: at k (lane l reads the 16
+// codes of unit j = 32 c + l at 16 j, 16-byte strides: conflict-free).  W4: a unit covers 32
+// codes, read as two 16-byte halves; with a plain layout the lanes' reads would be 32 bytes
+// apart (two-way bank conflicts on both reads).  So the 16-byte chunks are interleaved per
+// block of 32 units: half h of unit j = 32 b + l goes to chunk 64 b + h * nb + l (nb = the
+// block's unit count, 32 except in a row's last block), and a warp's read of one half is 32
+// consecutive chunks.
+template <int BITS>
+__host__ __device__ __forceinline__ int xs_chunk(int j, int h, int upr) {
+    if constexpr (BITS == 8) {
+        return j;
+    } else {
+        const int b = j >> 5;
+        const int nb = min(32, upr - 32 * b);
+        return 64 * b + h * nb + (j & 31);
+    }
+}
+template <int BITS>
+__host__ __device__ __forceinline__ int xs_byte(int k, int upr) {
+    if constexpr (BITS == 8)
+        return k;
+    else
+        return xs_chunk<BITS>(k >> 5, (k >> 4) & 1, upr) * 16 + (k & 15);
+}
+
 struct GemvArgs {
     const uint8_t *wq;
     const float *wscale;
@@ -120,12 +153,13 @@ struct GemvArgs {
 // Quantise the call's rows into xs (codes [MT][Kp], zero beyond M and K) and set s_scale /
 // s_rowsum.  TIn: __half or float; K and ldx are multiples of 16 / sizeof(TIn) and the rows
 // 16-byte aligned (gemv_can_fuse).
-template <int MT, typename TIn>
+template <int BITS, int MT, typename TIn>
 __device__ __forceinline__ void quantise_rows(const GemvArgs &p, uint8_t *xs, float *s_scale,
                                               int *s_rowsum, float (*s_red)[MT],
                                               int (*s_redi)[MT]) {
     constexpr int VEC = 16 / sizeof(TIn);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int upr = (BITS == 8 ? p.Kp : p.Kp / 2) / 16;  // 16-byte weight units per row
     const TIn *x = static_cast<const TIn *>(p.xin);
     const int nvec = p.K / VEC;
     auto widen = [](const uint4 &raw, float (&f)[VEC]) {
@@ -200,15 +234,17 @@ __device__ __forceinline__ void quantise_rows(const GemvArgs &p, uint8_t *xs, fl
                     }
                 }
             }
+            // VEC codes at k = v * VEC stay inside one 16-byte chunk of the layout
+            const int at = m * p.Kp + xs_byte<BITS>(v * VEC, upr);
             if constexpr (VEC == 8)
-                *reinterpret_cast<uint2 *>(xs + m * p.Kp + v * 8) = make_uint2(w[0], w[1]);
+                *reinterpret_cast<uint2 *>(xs + at) = make_uint2(w[0], w[1]);
             else
-                *reinterpret_cast<uint32_t *>(xs + m * p.Kp + v * 4) = w[0];
+                *reinterpret_cast<uint32_t *>(xs + at) = w[0];
         }
     }
     for (int i = p.K + tid; i < p.Kp; i += kThreads) {
 #pragma unroll
-        for (int m = 0; m < MT; m++) xs[m * p.Kp + i] = 0;
+        for (int m = 0; m < MT; m++) xs[m * p.Kp + xs_byte<BITS>(i, upr)] = 0;
     }
 #pragma unroll
     for (int m = 0; m < MT; m++) {
@@ -236,7 +272,8 @@ template <> struct OutsParam<true> { using type = OutputSet; };
 template <int BITS, int MT, bool SWIGLU, int U, bool SCATTER>
 __global__ void __launch_bounds__(kThreads, 1)
     gemv_kernel(const GemvArgs p, const typename OutsParam<SCATTER>::type outs) {
-    constexpr int NSEG = SWIGLU ? 2 : 1;
+    constexpr bool PAIR = gemv_paired(BITS, MT, SWIGLU);
+    constexpr int NSEG = SWIGLU || PAIR ? 2 : 1;
     constexpr int D = ring_depth(NSEG * U, MT);
     constexpr int V = MT;  // sums a warp reduces per row and segment
     extern __shared__ __align__(16) uint8_t smem[];
@@ -251,10 +288,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int nrows_out = SWIGLU ? p.N / 2 : p.N;
     const int r0 = blockIdx.x * p.rows_per_cta;
     const int nr = max(0, min(nrows_out, r0 + p.rows_per_cta) - r0);
-    const int my_rows = nr > warp ? (nr - warp + kWarps - 1) / kWarps : 0;
+    // PAIR: the CTA's rows in two halves, [0, h1) and [h1, nr); a task covers local row lr
+    // of both (the second half may be one row shorter)
+    const int h1 = PAIR ? (nr + 1) / 2 : nr;
+    const int my_rows = h1 > warp ? (h1 - warp + kWarps - 1) / kWarps : 0;
     const int ntask = my_rows * p.nch;
-    const uint8_t *seg0 = p.wq + (long long)r0 * row_bytes;                 // gate / only rows
-    const uint8_t *seg1 = p.wq + ((long long)p.N / 2 + r0) * row_bytes;     // up rows (swiglu)
+    const uint8_t *seg0 = p.wq + (long long)r0 * row_bytes;  // gate / only / first-half rows
+    const uint8_t *seg1 = p.wq + (PAIR ? (long long)(r0 + h1)        // second-half rows
+                                       : (long long)p.N / 2 + r0)    // up rows (swiglu)
+                                     * row_bytes;
 
     uint8_t *xs = smem;                                         // [MT][Kp] codes
     float *ws = reinterpret_cast<float *>(xs + (size_t)MT * p.Kp);  // [NSEG][rows_per_cta]
@@ -263,15 +305,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint4 ring[D][NSEG * U];
     auto issue = [&](int t, uint4 (&dst)[NSEG * U]) {
         const int i = t / p.nch, c = t - i * p.nch;
-        const long long off = (long long)(warp + i * kWarps) * row_bytes;
+        const int lr = warp + i * kWarps;
+        const long long off = (long long)lr * row_bytes;
         const int j0 = c * 32 * U + lane;
 #pragma unroll
         for (int s = 0; s < NSEG; s++) {
             const uint8_t *row = (s == 0 ? seg0 : seg1) + off;
+            const bool live = !PAIR || s == 0 || h1 + lr < nr;
 #pragma unroll
             for (int u = 0; u < U; u++) {
                 const int j = j0 + u * 32;
-                dst[s * U + u] = j < upr ? ldg_stream(row + j * 16) : make_uint4(0, 0, 0, 0);
+                dst[s * U + u] = live && j < upr ? ldg_stream(row + j * 16) : make_uint4(0, 0, 0, 0);
             }
         }
     };
@@ -288,17 +332,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------- activation codes
     asm volatile("griddepcontrol.wait;" ::: "memory");
     if (p.in_type == kF16) {
-        quantise_rows<MT, __half>(p, xs, s_scale, s_rowsum, s_red, s_redi);
+        quantise_rows<BITS, MT, __half>(p, xs, s_scale, s_rowsum, s_red, s_redi);
     } else if (p.in_type == kF32) {
-        quantise_rows<MT, float>(p, xs, s_scale, s_rowsum, s_red, s_redi);
+        quantise_rows<BITS, MT, float>(p, xs, s_scale, s_rowsum, s_red, s_redi);
     } else {
         const int8_t *codes = static_cast<const int8_t *>(p.xin);
         const int n16 = MT * p.Kp / 16;
+        const int row16 = p.Kp / 16;  // 16-byte chunks per row
         for (int i = tid; i < n16; i += kThreads) {
-            const int m = (i * 16) / p.Kp;
+            const int m = i / row16, c = i - m * row16;  // chunk c holds codes 16c .. 16c+15
             uint4 v = make_uint4(0, 0, 0, 0);
             if (m < p.M) v = *reinterpret_cast<const uint4 *>(codes + (long long)i * 16);
-            reinterpret_cast<uint4 *>(xs)[i] = v;
+            *reinterpret_cast<uint4 *>(xs + m * p.Kp + 16 * xs_chunk<BITS>(c >> (BITS == 8 ? 0 : 1),
+                                                                          c & 1, upr)) = v;
         }
         if (tid < MT) {
             s_scale[tid] = tid < p.M ? p.ascale[tid] : 0.0f;
@@ -340,11 +386,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                             // 16 packed bytes = 32 codes k = 32j .. 32j+31; word q covers 8
                             // codes: low nibbles k 8q..8q+3, high nibbles k 8q+4..8q+7.
                             const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+                            const int ca = 16 * xs_chunk<4>(j, 0, upr);
+                            const int cb = 16 * xs_chunk<4>(j, 1, upr);
 #pragma unroll
                             for (int m = 0; m < MT; m++) {
-                                const uint4 xa = *reinterpret_cast<const uint4 *>(xs + m * p.Kp + j * 32);
-                                const uint4 xb =
-                                    *reinterpret_cast<const uint4 *>(xs + m * p.Kp + j * 32 + 16);
+                                const uint4 xa = *reinterpret_cast<const uint4 *>(xs + m * p.Kp + ca);
+                                const uint4 xb = *reinterpret_cast<const uint4 *>(xs + m * p.Kp + cb);
                                 const uint32_t x8[8] = {xa.x, xa.y, xa.z, xa.w,
                                                         xb.x, xb.y, xb.z, xb.w};
                                 int a = acc[s][m];
@@ -390,11 +437,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     else
                         store_typed(p.out, p.out_type, (long long)m * p.ldc + n, y, 0);
                 } else {
-                    const float y = __fmul_rn(__fmul_rn(__int2float_rn(tot[0]), sa), ws[lr]);
-                    if constexpr (SCATTER)
-                        store_all(outs, p.out_type, (long long)m * p.ldc + n, y, tot[0]);
-                    else
-                        store_typed(p.out, p.out_type, (long long)m * p.ldc + n, y, tot[0]);
+#pragma unroll
+                    for (int s = 0; s < NSEG; s++) {
+                        const int l = s * h1 + lr;  // the CTA-local row of segment s
+                        if (s > 0 && l >= nr) break;
+                        const float y = __fmul_rn(__fmul_rn(__int2float_rn(tot[s]), sa), ws[l]);
+                        if constexpr (SCATTER)
+                            store_all(outs, p.out_type, (long long)m * p.ldc + n + s * h1, y,
+                                      tot[s]);
+                        else
+                            store_typed(p.out, p.out_type, (long long)m * p.ldc + n + s * h1, y,
+                                        tot[s]);
+                    }
                 }
             }
         }
@@ -418,7 +472,7 @@ inline bool plan(int rows, int Kp, int N, int bits, bool swiglu, int num_sms, Pl
     const int per = (nrows + num_sms - 1) / num_sms;
     const int upr = (bits == 8 ? Kp : Kp / 2) / 16;
     const int lane_units = (upr + 31) / 32;
-    const int maxu = swiglu ? kMaxUnitsSwiglu : kMaxUnits;
+    const int maxu = swiglu || gemv_paired(bits, mt_of(rows), swiglu) ? kMaxUnitsSwiglu : kMaxUnits;
     const int nch = (lane_units + maxu - 1) / maxu;
     const size_t smem = (size_t)mt_of(rows) * Kp + (size_t)(swiglu ? 2 : 1) * per * 4;
     if (smem > (size_t)kSmemBudget) return false;
@@ -486,7 +540,7 @@ cudaError_t launch_u(const WeightView &w, const GemvInput &in, int rows, const O
                      long long ldc, const Plan &pl, cudaStream_t stream) {
 #define QL_GEMV_U(u)                                                                      \
     case u:                                                                               \
-        if constexpr (!SWIGLU || u <= kMaxUnitsSwiglu)                                    \
+        if constexpr (!(SWIGLU || gemv_paired(BITS, MT, SWIGLU)) || u <= kMaxUnitsSwiglu) \
             return launch_t<BITS, MT, SWIGLU, u, SCATTER>(w, in, rows, out, out_type, ldc, pl, \
                                                              stream);                    \
         return cudaErrorInvalidValue;

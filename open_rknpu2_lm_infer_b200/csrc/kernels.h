@@ -117,12 +117,13 @@ cudaError_t launch_gemm(const WeightView &w, const CUtensorMap &wmap, const ActV
                         cudaStream_t stream);
 // SwiGLU in the GEMM's epilogue (gemm_glu.cu): w is an 8-bit gate/up matrix (N even, gate
 // columns first), wmap_glu its map from encode_glu_map (16-row boxes), plan from plan_gemm
-// without stream-K; out [rows][ldc] (ldc >= N/2) of kF16 or kF32 receives
+// (sk_ws as for launch_gemm); out [rows][ldc] (ldc >= N/2) of kF16 or kF32 receives
 // silu(y[m][j]) * y[m][N/2 + j].
 cudaError_t launch_gemm_glu(const WeightView &w, const CUtensorMap &wmap_glu, const ActView &a,
                             const CUtensorMap &amap, const CUtensorMap &amap_sub,
                             const GemmPlan &plan, int rows, void *out, int out_type,
-                            long long ldc, unsigned *err, bool pdl, cudaStream_t stream);
+                            long long ldc, unsigned *err, void *sk_ws, bool pdl,
+                            cudaStream_t stream);
 // The same with out.count > 1 (launch_gemm forwards to it): the split-N exchange's GEMM.
 cudaError_t launch_gemm_scatter(const WeightView &w, const CUtensorMap &wmap, const ActView &a,
                                 const CUtensorMap &amap, const CUtensorMap &amap_sub,

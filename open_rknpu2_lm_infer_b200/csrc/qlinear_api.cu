@@ -355,8 +355,7 @@ int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_
     // SwiGLU in the GEMM's epilogue: one output buffer, 8-bit prefill weights
     const bool glu = swiglu && w->has_glu && outs.count == 1 &&
                      !(b->flags & QLINEAR_BACKEND_SWIGLU_UNFUSED);
-    const GemmPlan plan =
-        plan_gemm(gv, rows, pairs, !glu && (b->flags & QLINEAR_BACKEND_GEMM_STREAM_K) != 0);
+    const GemmPlan plan = plan_gemm(gv, rows, pairs, (b->flags & QLINEAR_BACKEND_GEMM_STREAM_K) != 0);
     if ((st = ensure_sk(b, gemm_sk_bytes(plan)))) return st;
     if (plan.sk == 1) b->gemm_stream_k_calls++;
     const CUtensorMap *amap = nullptr;
@@ -374,7 +373,7 @@ int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_
         b->launches++;
     } else if (glu) {
         QL_TRY(launch_gemm_glu(gv, w->wmap_glu, av, *amap, *amap_sub, plan, rows, c_dev, c_type,
-                               ldc, b->d_err, true, stream));
+                               ldc, b->d_err, b->d_sk, true, stream));
         b->launches++;
         b->gemm_glu_calls++;
     } else {

@@ -115,3 +115,42 @@ def test_host_f32_swiglu_uses_fused_kernel(backends, coracle):
     assert fused_calls(fused) - before == 6
     lin.close()
     json.dumps(fused.stats())
+
+
+@pytest.mark.parametrize("bits,k,n,rows", [
+    (4, 2560, 2 * 9728, 16),   # cfg2 gate/up at 16 tokens: 76 tiles cut over every pair
+    (8, 1024, 2 * 1280, 64),   # 10 tiles, each cut into several segments
+    (4, 4096, 2 * 3584, 300),  # ragged token tiles
+])
+def test_fused_stream_k_matches_unfused(coracle, bits, k, n, rows):
+    """The SwiGLU epilogue on split tiles (stream-K): the tile's partial sums are summed in
+    the workspace and the finishing warp forms silu(g) * u; bit-identical to the unfused
+    path, repeatable (the workspace counters are left at zero)."""
+    fused = Backend(device=0, gemm_stream_k=True)
+    unfused = Backend(device=0, gemm_stream_k=True, swiglu_unfused=True)
+    try:
+        w = W.weight_codes(bits, k, n, stream=700 + rows)
+        sw = W.weight_scales(n, stream=700 + rows)
+        xh = W.activations(rows, k, stream=701 + rows)
+        a = torch.from_numpy(xh).cuda()
+        outs = []
+        for b in (fused, unfused):
+            lin = b.load(QuantMatrix(bits, k, n, w, sw))
+            sk0, f0 = b.stats()["gemm_stream_k_calls"], fused_calls(b)
+            res = []
+            for _ in range(2):
+                out = torch.zeros((rows, n // 2), dtype=torch.float16, device="cuda")
+                lin.run_device(a, out, rows, swiglu=True)
+                b.check()
+                res.append(out.cpu().numpy())
+            np.testing.assert_array_equal(res[0].view(np.uint16), res[1].view(np.uint16))
+            assert b.stats()["gemm_stream_k_calls"] - sk0 == 2
+            outs.append((res[0], fused_calls(b) - f0))
+            lin.close()
+        (got, nf), (ref, nu) = outs
+        assert nf == 2 and nu == 0
+        np.testing.assert_array_equal(got.view(np.uint16), ref.view(np.uint16))
+        compare(got.astype(np.float32), coracle.swiglu(coracle.linear(w, sw, xh)), 1e-3)
+    finally:
+        fused.close()
+        unfused.close()
