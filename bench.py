@@ -670,20 +670,19 @@ def run_sweep(args):
         downs = load(8, h, k, ncopy)
         for m in (1, 16, 128, 512, 4096):
             x = act(m, k)
-            mid = torch.empty((m, h), dtype=torch.float16, device=dev)
             y = torch.empty((m, k), dtype=torch.float16, device=dev)
 
             def chain():
                 for gu, dn in zip(gus, downs):
-                    gu.run_device(x, mid, m, swiglu=True, stream=stream)
-                    dn.run_device(mid, y, m, stream=stream)
+                    backend.run_mlp_device(gu, dn, x, y, m, stream=stream)
             b0 = backend.launches()
             secs = time_chain(chain) / ncopy
             launches = (backend.launches() - b0) / (7 * ncopy)
             ops = 2.0 * m * k * 2 * h + 2.0 * m * h * k
             bytes_ = (kernel_bytes(4, k, 2 * h, m) + kernel_bytes(8, h, k, m)
                       + 2 * m * k + 2 * m * h + 2 * m * h + 2 * m * k)
-            emit("cfg2 MLP block W4 gate/up+SwiGLU -> W8 down", m, secs, ops, bytes_, launches,
+            emit("cfg2 MLP block W4 gate/up+SwiGLU -> W8 down (qlinear_run_mlp_device)", m, secs,
+                 ops, bytes_, launches,
                  {"copies": ncopy})
         for lin in gus + downs:
             lin.close()
@@ -702,18 +701,16 @@ def run_sweep(args):
         n_w4 = sum(b == 4 for row in draw for b in row)
         for m in (1, 512):
             xs = {k: act(m, k, stream_id=k) for k in (2560, 4096)}
-            outs = {n: torch.empty((m, n), dtype=torch.float16, device=dev)
-                    for n in (6144, 2560, 9728)}
+            outs = {n: torch.empty((m, n), dtype=torch.float16, device=dev) for n in (6144, 2560)}
 
             def chain():
                 for layer in layers:
-                    for lname, bits, k, n, lin in layer:
-                        if lname == "gate_up":
-                            lin.run_device(xs[2560], outs[9728], m, swiglu=True, stream=stream)
-                        elif lname == "down":
-                            lin.run_device(outs[9728], outs[2560], m, stream=stream)
-                        else:
-                            lin.run_device(xs[k], outs[n], m, stream=stream)
+                    lins = {lname: lin for lname, _, _, _, lin in layer}
+                    lins["qkv"].run_device(xs[2560], outs[6144], m, stream=stream)
+                    lins["o"].run_device(xs[4096], outs[2560], m, stream=stream)
+                    # the MLP block: gate/up + SwiGLU -> f32 middle -> down
+                    backend.run_mlp_device(lins["gate_up"], lins["down"], xs[2560], outs[2560], m,
+                                           stream=stream)
             b0 = backend.launches()
             secs = time_chain(chain, reps=3)
             launches = (backend.launches() - b0) / 5

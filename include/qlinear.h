@@ -114,7 +114,10 @@ QLINEAR_API void qlinear_backend_config_init(qlinear_backend_config *cfg);
 
 /* Replaces rk_npu_open + rk_npu_iommu_domain_create (src/npu.rs:310-366). */
 QLINEAR_API qlinear_backend *qlinear_backend_create(const qlinear_backend_config *cfg);
-/* Replaces rk_npu_iommu_domain_free + rk_npu_close (Handle drop, src/npu.rs:133-137). */
+/* Replaces rk_npu_iommu_domain_free + rk_npu_close (Handle drop, src/npu.rs:133-137).
+ * Releases the caller's handle; every weights object holds its backend (as the reference's
+ * Linear holds a Backend clone, src/npu.rs:252-260), so the device resources go when the
+ * handle and the last weights object of the backend have both been freed, in either order. */
 QLINEAR_API void qlinear_backend_free(qlinear_backend *backend);
 
 /* Replaces rk_npu_w4a8_weights_create (src/npu.rs:395-402) for bits == 4 and
@@ -175,6 +178,20 @@ QLINEAR_API int qlinear_run_f32_ex(qlinear_backend *backend, const qlinear_weigh
 QLINEAR_API int qlinear_run_device(qlinear_backend *backend, const qlinear_weights *weights,
                        const void *a_dev, int a_type, void *c_dev, int c_type, long long ldc,
                        int rows, unsigned flags, void *stream);
+
+/* The MLP block of a decoder layer, replacing the two calls of src/model/dense.rs:499-530
+ * (gate_up.run_swiglu(normalized -> middle), then down.run(middle -> projected)):
+ * c_dev [rows][ldc] (ldc >= N of down) = down(silu(g) * u) with [g | u] = gate_up(a_dev), the
+ * [rows][N/2] middle kept in f32 as in the reference (so the result is that of the two calls
+ * with an f32 middle, bit for bit).  gate_up: N even, gate columns first; down: K = N/2 of
+ * gate_up.  a_type / c_type: QLINEAR_F16 or QLINEAR_F32.  The middle lives in a backend
+ * scratch buffer; the two GEMV/GEMM calls run back to back, the second one's weight stream
+ * starting while the first drains.  Asynchronous on `stream`; the same ordering rule as
+ * qlinear_run_device. */
+QLINEAR_API int qlinear_run_mlp_device(qlinear_backend *backend, const qlinear_weights *gate_up,
+                                       const qlinear_weights *down, const void *a_dev,
+                                       int a_type, void *c_dev, int c_type, long long ldc,
+                                       int rows, void *stream);
 
 /* Split-N output exchange fused into the kernels (no reference counterpart; one process per
  * GPU, the layer's output columns sharded over the GPUs of one node): like

@@ -267,16 +267,20 @@ struct NoOutputs {};
 template <bool SCATTER> struct OutsParam { using type = NoOutputs; };
 template <> struct OutsParam<true> { using type = OutputSet; };
 
-// BITS: 4/8.  MT: activation rows held (>= M).  U: 16-byte units per lane per task segment.
-// SCATTER: store every output element to each of outs' destinations.
-template <int BITS, int MT, bool SWIGLU, int U, bool SCATTER>
-__global__ void __launch_bounds__(kThreads, 1)
-    gemv_kernel(const GemvArgs p, const typename OutsParam<SCATTER>::type outs) {
+// The GEMV of one call, run by every CTA of the grid.  BITS: 4/8.  MT: activation rows held
+// (>= M).  U: 16-byte units per lane per task segment.  SCATTER: store every output element
+// to each of outs' destinations.  smem: this call's dynamic shared memory (codes [MT][Kp],
+// then the weight scales).  wait(): called by every thread after the first weight loads are
+// issued and before the activations are read; returns false to abandon the call (the
+// loads in flight are plain loads into registers and need no draining).
+template <int BITS, int MT, bool SWIGLU, int U, bool SCATTER, typename Wait>
+__device__ __forceinline__ void gemv_body(const GemvArgs &p,
+                                          const typename OutsParam<SCATTER>::type &outs,
+                                          uint8_t *smem, Wait &&wait) {
     constexpr bool PAIR = gemv_paired(BITS, MT, SWIGLU);
     constexpr int NSEG = SWIGLU || PAIR ? 2 : 1;
     constexpr int D = ring_depth(NSEG * U, MT);
     constexpr int V = MT;  // sums a warp reduces per row and segment
-    extern __shared__ __align__(16) uint8_t smem[];
     __shared__ float s_scale[MT];
     __shared__ int s_rowsum[MT];
     __shared__ float s_red[kWarps][MT];
@@ -330,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     // ---------------------------------------------------------------- activation codes
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (!wait()) return;
     if (p.in_type == kF16) {
         quantise_rows<BITS, MT, __half>(p, xs, s_scale, s_rowsum, s_red, s_redi);
     } else if (p.in_type == kF32) {
@@ -455,6 +459,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // peers' copies of the output: visible system-wide before the next work on this stream
     if constexpr (SCATTER) __threadfence_system();
+}
+
+template <int BITS, int MT, bool SWIGLU, int U, bool SCATTER>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemv_kernel(const GemvArgs p, const typename OutsParam<SCATTER>::type outs) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    gemv_body<BITS, MT, SWIGLU, U, SCATTER>(p, outs, smem, [] {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        return true;
+    });
 }
 
 inline int mt_of(int rows) { return rows <= 1 ? 1 : rows <= 2 ? 2 : rows <= 4 ? 4 : 8; }

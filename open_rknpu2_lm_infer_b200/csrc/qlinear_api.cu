@@ -32,6 +32,10 @@
 using namespace ql;
 
 struct qlinear_backend {
+    // the caller's handle plus one per live weights object: weights keep their backend alive,
+    // like the reference's Linear holding a Backend clone (src/npu.rs:252-260), so weights
+    // freed after the backend handle still find it
+    int refs = 1;
     int device = 0;
     int round_mode = QLINEAR_ROUND_AWAY;
     unsigned flags = 0;
@@ -49,6 +53,10 @@ struct qlinear_backend {
     // f32 gate/up scratch for SwiGLU through the GEMM
     float *d_y = nullptr;
     size_t y_elems = 0;
+    // the MLP block's f32 intermediate [rows][N/2] (qlinear_run_mlp_device)
+    float *d_mid = nullptr;
+    size_t mid_bytes = 0;
+    unsigned long long mlp_calls = 0;
     // stream-K partial sums and contribution counters of the GEMM (counters zero between
     // launches)
     void *d_sk = nullptr;
@@ -468,6 +476,7 @@ qlinear_weights *weights_create_common(qlinear_backend *b, const qlinear_weight_
     }
     b->weight_bytes += w->bytes;
     (v.bits == 4 ? b->loaded_w4 : b->loaded_w8)++;
+    b->refs++;
     b->max_kp = std::max(b->max_kp, v.Kp);
     b->max_n = std::max(b->max_n, v.N);
     return w;
@@ -535,14 +544,15 @@ qlinear_backend *qlinear_backend_create(const qlinear_backend_config *cfg) {
     return b;
 }
 
-void qlinear_backend_free(qlinear_backend *b) {
-    if (!b) return;
+namespace {
+void destroy_backend(qlinear_backend *b) {
     DeviceGuard guard(b->device);
     if (b->stream) cudaStreamSynchronize(b->stream);
     cudaFree(b->d_ws);
     cudaFree(b->d_ascale);
     cudaFree(b->d_rowsum);
     cudaFree(b->d_y);
+    cudaFree(b->d_mid);
     cudaFree(b->d_sk);
     cudaFree(b->d_in);
     cudaFree(b->d_out);
@@ -556,6 +566,11 @@ void qlinear_backend_free(qlinear_backend *b) {
         for (auto x : e) cudaEventDestroy(x);
     if (b->stream) cudaStreamDestroy(b->stream);
     delete b;
+}
+}  // namespace
+
+void qlinear_backend_free(qlinear_backend *b) {
+    if (b && --b->refs == 0) destroy_backend(b);
 }
 
 qlinear_weights *qlinear_weights_create(qlinear_backend *b, const qlinear_weight_config *cfg,
@@ -604,6 +619,7 @@ void qlinear_weights_free(qlinear_weights *w) {
     b->weight_bytes -= w->bytes;
     (w->view.bits == 4 ? b->loaded_w4 : b->loaded_w8)--;
     delete w;
+    if (--b->refs == 0) destroy_backend(b);  // the backend handle was freed before
 }
 
 int qlinear_backend_prepare(qlinear_backend *b, int rows) {
@@ -626,6 +642,32 @@ int qlinear_run_device(qlinear_backend *b, const qlinear_weights *w, const void 
     DeviceGuard guard(b->device);
     return run_device_impl(b, w, a_dev, a_type, single_output(c_dev), c_type, ldc, rows, flags,
                            static_cast<cudaStream_t>(stream));
+}
+
+int qlinear_run_mlp_device(qlinear_backend *b, const qlinear_weights *gate_up,
+                           const qlinear_weights *down, const void *a_dev, int a_type, void *c_dev,
+                           int c_type, long long ldc, int rows, void *stream) {
+    if (!b || !gate_up || !down || gate_up->backend != b || down->backend != b)
+        return QLINEAR_ERR_PARAM;
+    const WeightView &gu = gate_up->view, &dn = down->view;
+    if (gu.N % 2 != 0 || dn.K != gu.N / 2 || rows < 1 || !a_dev || !c_dev ||
+        !valid_io_type(a_type) || !valid_io_type(c_type) || ldc < dn.N)
+        return QLINEAR_ERR_PARAM;
+    DeviceGuard guard(b->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int h = gu.N / 2;
+    int st = ensure_dev(reinterpret_cast<void **>(&b->d_mid), &b->mid_bytes,
+                        (size_t)rows * h * sizeof(float));
+    if (st) return st;
+    b->mlp_calls++;
+    // gate/up with the SiLU-gated product into the f32 intermediate, then down (each call
+    // launched with programmatic stream serialization, so the down call's weight stream
+    // starts while the gate/up call drains)
+    st = run_device_impl(b, gate_up, a_dev, a_type, single_output(b->d_mid), QLINEAR_F32, h, rows,
+                         QLINEAR_RUN_SWIGLU, s);
+    if (st) return st;
+    return run_device_impl(b, down, b->d_mid, QLINEAR_F32, single_output(c_dev), c_type, ldc, rows,
+                           0, s);
 }
 
 int qlinear_run_device_scatter(qlinear_backend *b, const qlinear_weights *w, const void *a_dev,
@@ -871,7 +913,7 @@ int qlinear_selftest_wait_timeout(qlinear_backend *b, unsigned long long limit_n
 int qlinear_backend_stats(const qlinear_backend *b, char *buf, size_t len) {
     if (!b) return QLINEAR_ERR_PARAM;
     const size_t ws = b->ws_bytes + b->ws_rows * 8 + b->y_elems + b->d_in_bytes + b->d_out_bytes;
-    char tmp[1024];
+    char tmp[2048];
     const int n = std::snprintf(
         tmp, sizeof(tmp),
         "{\"backend\": \"cuda-sm100a\", \"device\": %d, \"sm_count\": %d, \"loaded_w4\": %d, "
@@ -881,13 +923,14 @@ int qlinear_backend_stats(const qlinear_backend *b, char *buf, size_t len) {
         "\"strategy_fallback_calls\": 0, \"weight_reload_calls\": 0, \"round_mode\": \"%s\", "
         "\"prepared_rows\": %d, \"kernel_launches\": %llu, \"gemv_calls\": %llu, "
         "\"gemm_calls\": %llu, \"gemm_stream_k_calls\": %llu, \"gemm_swiglu_fused_calls\": %llu, "
+        "\"mlp_calls\": %llu, "
         "\"gemm_pairs_resident\": [%d, %d]}",
         b->device, b->num_sms, b->loaded_w4, b->loaded_w8, (unsigned long long)b->weight_bytes,
         (unsigned long long)ws, b->ws_bytes ? 1 : 0,
         (unsigned long long)(b->h_in_bytes + b->h_out_bytes),
         b->round_mode == QLINEAR_ROUND_AWAY ? "away" : "even", b->prepared_rows, b->launches,
-        b->gemv_calls, b->gemm_calls, b->gemm_stream_k_calls, b->gemm_glu_calls, b->gemm_pairs[0],
-        b->gemm_pairs[1]);
+        b->gemv_calls, b->gemm_calls, b->gemm_stream_k_calls, b->gemm_glu_calls, b->mlp_calls,
+        b->gemm_pairs[0], b->gemm_pairs[1]);
     if (n < 0) return QLINEAR_ERR_PARAM;
     if (buf && len) {
         std::strncpy(buf, tmp, len - 1);

@@ -227,6 +227,22 @@ class Backend:
         status, QLINEAR_ERR_TIMEOUT when the path works."""
         return int(self._lib.qlinear_selftest_wait_timeout(self.raw, int(limit_s * 1e9)))
 
+    def run_mlp_device(self, gate_up: "Linear", down: "Linear", a, out, rows: int,
+                       ldc: int | None = None, stream=None) -> None:
+        """The MLP block of src/model/dense.rs:499-530 on device buffers: out = down(silu(g) *
+        u), [g | u] = gate_up(a), with the reference's f32 middle; one fused launch for a
+        single row (qlinear_run_mlp_device)."""
+        def code(t):
+            s = str(getattr(t, "dtype", ""))
+            if "float16" in s:
+                return L.F16
+            if "float32" in s:
+                return L.F32
+            raise TypeError(s)
+        _check(self._lib.qlinear_run_mlp_device(
+            self.raw, gate_up._raw, down._raw, _ptr(a), code(a), _ptr(out), code(out),
+            down.n() if ldc is None else ldc, rows, stream), "MLP device run")
+
     def act_quant_device(self, a, rows: int, k: int, codes, scales, rowsums=None,
                          stream=None) -> None:
         """Activation quantisation alone (device buffers); exports the int8 codes."""

@@ -269,3 +269,28 @@ def test_w4_default_keeps_int8_copy(backend):
     k, n = 512, 256
     lin = backend.load(QuantMatrix(4, k, n, W.weight_codes(4, k, n), W.weight_scales(n)))
     assert lin.device_bytes >= k * n + k * n // 2
+
+
+def test_weights_outlive_backend_handle():
+    """Weights keep their backend alive (src/npu.rs:252-260): freeing the backend handle first
+    and the weights afterwards -- or leaving the weights to interpreter exit -- is safe."""
+    import subprocess
+    import sys
+    from open_rknpu2_lm_infer_b200 import Backend
+    b = Backend(device=0)
+    codes, scales = W.kat_matrix(8)
+    lin = b.load(QuantMatrix(8, 256, 256, codes, scales))
+    b.close()
+    lin.close()
+    script = (
+        "from open_rknpu2_lm_infer_b200 import Backend, QuantMatrix\n"
+        "from open_rknpu2_lm_infer_b200 import workloads as W\n"
+        "b = Backend(device=0)\n"
+        "c, s = W.kat_matrix(4)\n"
+        "keep = b.load(QuantMatrix(4, 256, 256, c, s))\n"
+        "b.close()\n")
+    import os
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", script], cwd=root, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
