@@ -60,7 +60,7 @@ def test_sharded_equals_single_gpu(tmp_path):
     script = tmp_path / "child.py"
     script.write_text(CHILD)
     env = dict(os.environ, QL_ROOT=ROOT, NCCL_NVLS_ENABLE="0")
-    n = min(torch.cuda.device_count(), 4)
+    n = min(torch.cuda.device_count(), 8)
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run",
            "--nnodes=1", f"--nproc-per-node={n}", "--master-addr", "127.0.0.1",
            "--master-port", "29531", str(script)]
