@@ -55,6 +55,18 @@ __host__ __device__ constexpr bool gemv_paired(int bits, int mt, bool swiglu) {
     return !swiglu && (bits == 4 ? mt >= 4 : mt >= 8);
 }
 
+// Balanced mode (BAL, one or two activation rows, one output buffer): a CTA's rows are cut
+// into nch chunks and each of its 16 warps takes a contiguous range of the row-major
+// (row, chunk) task list, instead of whole rows (66 rows per CTA for N = 9728 left 2 warps
+// streaming a fifth row while 14 waited).  A warp reduces its sums only where a row ends or
+// its range ends (a row split between two warps), and adds them into shared memory (int32
+// atomics: exact in any order); a pass after a CTA barrier forms the outputs.  (Dealing the
+// tasks round-robin instead measured 2x slower: a warp's consecutive tasks then belong to
+// different rows, and the shuffle reduction after every 512-byte task stalled it.)
+// Smaller tasks, so the ring is deeper: about 20 units per lane in flight, as in the
+// whole-row mode.  plan() chooses it only where whole rows are badly uneven.
+__host__ __device__ constexpr int bal_depth(int units) { return 20 / units < 1 ? 1 : 20 / units; }
+
 // Register ring depth for NSEG*U units per lane per task: about 96 data registers per thread
 // with one or two activation rows, less with more (their partial sums need registers too).
 __host__ __device__ constexpr int ring_depth(int units, int mt) {
@@ -273,13 +285,13 @@ template <> struct OutsParam<true> { using type = OutputSet; };
 // then the weight scales).  wait(): called by every thread after the first weight loads are
 // issued and before the activations are read; returns false to abandon the call (the
 // loads in flight are plain loads into registers and need no draining).
-template <int BITS, int MT, bool SWIGLU, int U, bool SCATTER, typename Wait>
+template <int BITS, int MT, bool SWIGLU, int U, bool SCATTER, bool BAL, typename Wait>
 __device__ __forceinline__ void gemv_body(const GemvArgs &p,
                                           const typename OutsParam<SCATTER>::type &outs,
                                           uint8_t *smem, Wait &&wait) {
     constexpr bool PAIR = gemv_paired(BITS, MT, SWIGLU);
     constexpr int NSEG = SWIGLU || PAIR ? 2 : 1;
-    constexpr int D = ring_depth(NSEG * U, MT);
+    constexpr int D = BAL ? bal_depth(NSEG * U) : ring_depth(NSEG * U, MT);
     constexpr int V = MT;  // sums a warp reduces per row and segment
     __shared__ float s_scale[MT];
     __shared__ int s_rowsum[MT];
@@ -296,7 +308,23 @@ __device__ __forceinline__ void gemv_body(const GemvArgs &p,
     // of both (the second half may be one row shorter)
     const int h1 = PAIR ? (nr + 1) / 2 : nr;
     const int my_rows = h1 > warp ? (h1 - warp + kWarps - 1) / kWarps : 0;
-    const int ntask = my_rows * p.nch;
+    // Task t of this warp: whole-row mode, local row warp + (t / nch) * kWarps and chunk
+    // t % nch; balanced mode, CTA task T = tb + t = row * nch + chunk, [tb, te) this warp's
+    // share of the h1 * nch tasks.
+    const int tb = BAL ? (int)((long long)warp * h1 * p.nch / kWarps) : 0;
+    const int te = BAL ? (int)((long long)(warp + 1) * h1 * p.nch / kWarps) : 0;
+    const int ntask = BAL ? te - tb : my_rows * p.nch;
+    auto task_of = [&](int t, int &lr, int &c) {
+        if constexpr (BAL) {
+            const int T = tb + t;
+            lr = T / p.nch;
+            c = T - lr * p.nch;
+        } else {
+            const int i = t / p.nch;
+            c = t - i * p.nch;
+            lr = warp + i * kWarps;
+        }
+    };
     const uint8_t *seg0 = p.wq + (long long)r0 * row_bytes;  // gate / only / first-half rows
     const uint8_t *seg1 = p.wq + (PAIR ? (long long)(r0 + h1)        // second-half rows
                                        : (long long)p.N / 2 + r0)    // up rows (swiglu)
@@ -304,12 +332,13 @@ __device__ __forceinline__ void gemv_body(const GemvArgs &p,
 
     uint8_t *xs = smem;                                         // [MT][Kp] codes
     float *ws = reinterpret_cast<float *>(xs + (size_t)MT * p.Kp);  // [NSEG][rows_per_cta]
+    // balanced mode: the rows' sums [NSEG][rows_per_cta][MT]
+    int *s_acc = reinterpret_cast<int *>(ws + (SWIGLU ? 2 : 1) * p.rows_per_cta);
 
-    // Task t of this warp: local row warp + (t / nch) * kWarps, chunk t % nch.
     uint4 ring[D][NSEG * U];
     auto issue = [&](int t, uint4 (&dst)[NSEG * U]) {
-        const int i = t / p.nch, c = t - i * p.nch;
-        const int lr = warp + i * kWarps;
+        int lr, c;
+        task_of(t, lr, c);
         const long long off = (long long)lr * row_bytes;
         const int j0 = c * 32 * U + lane;
 #pragma unroll
@@ -331,6 +360,10 @@ __device__ __forceinline__ void gemv_body(const GemvArgs &p,
     for (int i = tid; i < nr; i += kThreads) {
         ws[i] = p.wscale[r0 + i];
         if (SWIGLU) ws[p.rows_per_cta + i] = p.wscale[p.N / 2 + r0 + i];
+    }
+
+    if constexpr (BAL) {  // zeroed before the prologue's barriers
+        for (int i = tid; i < NSEG * p.rows_per_cta * MT; i += kThreads) s_acc[i] = 0;
     }
 
     // ---------------------------------------------------------------- activation codes
@@ -357,6 +390,37 @@ __device__ __forceinline__ void gemv_body(const GemvArgs &p,
     }
     __syncthreads();
 
+    // Row lr's outputs for activation row m from its int32 totals (W4: minus 8 * sum(q)).
+    auto emit_row = [&](int (&tot)[NSEG], int m, int lr) {
+        if (BITS == 4) {
+#pragma unroll
+            for (int s = 0; s < NSEG; s++) tot[s] -= 8 * s_rowsum[m];
+        }
+        const int n = r0 + lr;
+        const float sa = s_scale[m];
+        if constexpr (SWIGLU) {
+            const float g = __fmul_rn(__fmul_rn(__int2float_rn(tot[0]), sa), ws[lr]);
+            const float up = __fmul_rn(__fmul_rn(__int2float_rn(tot[NSEG - 1]), sa),
+                                       ws[p.rows_per_cta + lr]);
+            const float y = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), up);
+            if constexpr (SCATTER)
+                store_all(outs, p.out_type, (long long)m * p.ldc + n, y, 0);
+            else
+                store_typed(p.out, p.out_type, (long long)m * p.ldc + n, y, 0);
+        } else {
+#pragma unroll
+            for (int s = 0; s < NSEG; s++) {
+                const int l = s * h1 + lr;  // the CTA-local row of segment s
+                if (s > 0 && l >= nr) break;
+                const float y = __fmul_rn(__fmul_rn(__int2float_rn(tot[s]), sa), ws[l]);
+                if constexpr (SCATTER)
+                    store_all(outs, p.out_type, (long long)m * p.ldc + n + s * h1, y, tot[s]);
+                else
+                    store_typed(p.out, p.out_type, (long long)m * p.ldc + n + s * h1, y, tot[s]);
+            }
+        }
+    };
+
     // ---------------------------------------------------------------- stream the weights
     int acc[NSEG][V];
 #pragma unroll
@@ -368,7 +432,8 @@ __device__ __forceinline__ void gemv_body(const GemvArgs &p,
         for (int d = 0; d < D; d++) {
             const int t = t0 + d;
             if (t >= ntask) break;
-            const int i = t / p.nch, c = t - i * p.nch;
+            int lr, c;
+            task_of(t, lr, c);
             const int j0 = c * 32 * U + lane;
 #pragma unroll
             for (int u = 0; u < U; u++) {
@@ -411,10 +476,10 @@ __device__ __forceinline__ void gemv_body(const GemvArgs &p,
                 }
             }
             if (t + D < ntask) issue(t + D, ring[d]);  // refill the slot just consumed
-            if (c != p.nch - 1) continue;              // the row has more chunks
+            // the row has more chunks (balanced mode: in this warp's range)
+            if (c != p.nch - 1 && (!BAL || t != ntask - 1)) continue;
 
             // ---------------------------------------------------------- row epilogue
-            const int lr = warp + i * kWarps;
             int tot[NSEG];
 #pragma unroll
             for (int s = 0; s < NSEG; s++) {
@@ -425,47 +490,36 @@ __device__ __forceinline__ void gemv_body(const GemvArgs &p,
             }
             const int m = lane / (32 / V);  // activation row whose totals this lane holds
             if ((lane % (32 / V)) == 0 && m < p.M) {
-                if (BITS == 4) {
+                if constexpr (BAL) {
 #pragma unroll
-                    for (int s = 0; s < NSEG; s++) tot[s] -= 8 * s_rowsum[m];
-                }
-                const int n = r0 + lr;
-                const float sa = s_scale[m];
-                if constexpr (SWIGLU) {
-                    const float g = __fmul_rn(__fmul_rn(__int2float_rn(tot[0]), sa), ws[lr]);
-                    const float up = __fmul_rn(__fmul_rn(__int2float_rn(tot[NSEG - 1]), sa),
-                                               ws[p.rows_per_cta + lr]);
-                    const float y = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), up);
-                    if constexpr (SCATTER)
-                        store_all(outs, p.out_type, (long long)m * p.ldc + n, y, 0);
-                    else
-                        store_typed(p.out, p.out_type, (long long)m * p.ldc + n, y, 0);
+                    for (int s = 0; s < NSEG; s++)
+                        atomicAdd(&s_acc[(s * p.rows_per_cta + lr) * MT + m], tot[s]);
                 } else {
-#pragma unroll
-                    for (int s = 0; s < NSEG; s++) {
-                        const int l = s * h1 + lr;  // the CTA-local row of segment s
-                        if (s > 0 && l >= nr) break;
-                        const float y = __fmul_rn(__fmul_rn(__int2float_rn(tot[s]), sa), ws[l]);
-                        if constexpr (SCATTER)
-                            store_all(outs, p.out_type, (long long)m * p.ldc + n + s * h1, y,
-                                      tot[s]);
-                        else
-                            store_typed(p.out, p.out_type, (long long)m * p.ldc + n + s * h1, y,
-                                        tot[s]);
-                    }
+                    emit_row(tot, m, lr);
                 }
             }
+        }
+    }
+    if constexpr (BAL) {  // every task's sums are in s_acc: form the outputs
+        __syncthreads();
+        for (int e = tid; e < h1 * MT; e += kThreads) {
+            const int lr = e / MT, m = e - lr * MT;
+            if (m >= p.M) continue;
+            int tot[NSEG];
+#pragma unroll
+            for (int s = 0; s < NSEG; s++) tot[s] = s_acc[(s * p.rows_per_cta + lr) * MT + m];
+            emit_row(tot, m, lr);
         }
     }
     // peers' copies of the output: visible system-wide before the next work on this stream
     if constexpr (SCATTER) __threadfence_system();
 }
 
-template <int BITS, int MT, bool SWIGLU, int U, bool SCATTER>
+template <int BITS, int MT, bool SWIGLU, int U, bool SCATTER, bool BAL>
 __global__ void __launch_bounds__(kThreads, 1)
     gemv_kernel(const GemvArgs p, const typename OutsParam<SCATTER>::type outs) {
     extern __shared__ __align__(16) uint8_t smem[];
-    gemv_body<BITS, MT, SWIGLU, U, SCATTER>(p, outs, smem, [] {
+    gemv_body<BITS, MT, SWIGLU, U, SCATTER, BAL>(p, outs, smem, [] {
         asm volatile("griddepcontrol.wait;" ::: "memory");
         return true;
     });
@@ -476,10 +530,14 @@ inline int mt_of(int rows) { return rows <= 1 ? 1 : rows <= 2 ? 2 : rows <= 4 ? 
 struct Plan {
     int rows_per_cta, grid, nch, units;
     size_t smem;
+    bool bal;  // balanced (row, chunk) tasks; units then 1, 2 or 4
 };
 
 // Rows per CTA (one CTA per SM), chunks per row and units per lane, shared memory.
-inline bool plan(int rows, int Kp, int N, int bits, bool swiglu, int num_sms, Plan *pl) {
+// allow_bal: the caller launches the single-output kernel (the balanced mode is built only
+// for that, at one or two activation rows).
+inline bool plan(int rows, int Kp, int N, int bits, bool swiglu, int num_sms, Plan *pl,
+                 bool allow_bal = false) {
     if (rows < 1 || rows > 8 || num_sms < 1) return false;
     const int nrows = swiglu ? N / 2 : N;
     if (nrows < 1) return false;
@@ -495,10 +553,38 @@ inline bool plan(int rows, int Kp, int N, int bits, bool swiglu, int num_sms, Pl
     pl->nch = nch;
     pl->units = round_units((lane_units + nch - 1) / nch);
     pl->smem = smem;
+    pl->bal = false;
+    if (allow_bal && mt_of(rows) <= 2) {
+        // time ~ the busiest warp's units per lane: whole rows, ceil(per / 16) rows of nch
+        // chunks of `units`; balanced, ceil(per * nchb / 16) tasks of u units
+        const long long whole = (long long)((per + kWarps - 1) / kWarps) * nch * pl->units;
+        long long best = whole;
+        int bu = 0;
+        for (int u : {4, 2, 1}) {
+            const int nchb = (lane_units + u - 1) / u;
+            const long long cost = (long long)(((long long)per * nchb + kWarps - 1) / kWarps) * u;
+            if (cost < best) { best = cost; bu = u; }
+        }
+        // Only where whole rows leave the warps badly uneven (a busiest warp with >= 1.4x
+        // the units of the balanced split: the 2560-wide projections' 18 rows per CTA).
+        // Measured on B200, the balanced mode's small tasks cost more issue slots per byte:
+        // cfg1 (66 rows per CTA, predicted 25 -> 21) ran 9.1 -> 10.9 us per call, cfg4 W4
+        // M=1 (194 rows, 104 -> 97) 30.1 -> 58.5 us.
+        if (bu && 10 * best * 14 <= 100 * whole) {
+            const int nseg = swiglu ? 2 : 1;
+            const size_t smem_b = smem + (size_t)nseg * per * mt_of(rows) * 4;
+            if (smem_b <= (size_t)kSmemBudget) {
+                pl->bal = true;
+                pl->units = bu;
+                pl->nch = (lane_units + bu - 1) / bu;
+                pl->smem = smem_b;
+            }
+        }
+    }
     return true;
 }
 
-template <int BITS, int MT, bool SWIGLU, int U, bool SCATTER>
+template <int BITS, int MT, bool SWIGLU, int U, bool SCATTER, bool BAL = false>
 cudaError_t launch_t(const WeightView &w, const GemvInput &in, int rows, const OutputSet &out, int out_type,
                      long long ldc, const Plan &pl, cudaStream_t stream) {
     GemvArgs a{};
@@ -522,7 +608,7 @@ cudaError_t launch_t(const WeightView &w, const GemvInput &in, int rows, const O
     a.rows_per_cta = pl.rows_per_cta;
     a.nch = pl.nch;
     a.err = in.err;
-    auto kern = gemv_kernel<BITS, MT, SWIGLU, U, SCATTER>;
+    auto kern = gemv_kernel<BITS, MT, SWIGLU, U, SCATTER, BAL>;
     static int configured[64] = {0};  // per device: raise the opt-in limit once
     int dev = 0;
     cudaGetDevice(&dev);
@@ -558,6 +644,17 @@ cudaError_t launch_u(const WeightView &w, const GemvInput &in, int rows, const O
             return launch_t<BITS, MT, SWIGLU, u, SCATTER>(w, in, rows, out, out_type, ldc, pl, \
                                                              stream);                    \
         return cudaErrorInvalidValue;
+    if constexpr (MT <= 2 && !SCATTER) {
+        if (pl.bal) {
+            switch (pl.units) {
+            case 1: return launch_t<BITS, MT, SWIGLU, 1, false, true>(w, in, rows, out, out_type, ldc, pl, stream);
+            case 2: return launch_t<BITS, MT, SWIGLU, 2, false, true>(w, in, rows, out, out_type, ldc, pl, stream);
+            case 4: return launch_t<BITS, MT, SWIGLU, 4, false, true>(w, in, rows, out, out_type, ldc, pl, stream);
+            default: return cudaErrorInvalidValue;
+            }
+        }
+    }
+    if (pl.bal) return cudaErrorInvalidValue;
     switch (pl.units) {
         QL_GEMV_U(1) QL_GEMV_U(2) QL_GEMV_U(3) QL_GEMV_U(4) QL_GEMV_U(5)
         QL_GEMV_U(6) QL_GEMV_U(8) QL_GEMV_U(10) QL_GEMV_U(12) QL_GEMV_U(16)
@@ -583,7 +680,7 @@ cudaError_t launch_checked(const WeightView &w, const GemvInput &in, int rows, c
                            int out_type, long long ldc, bool swiglu, int num_sms,
                            cudaStream_t stream) {
     Plan pl;
-    if (!plan(rows, w.Kp, w.N, w.bits, swiglu, num_sms, &pl)) return cudaErrorInvalidValue;
+    if (!plan(rows, w.Kp, w.N, w.bits, swiglu, num_sms, &pl, !SCATTER)) return cudaErrorInvalidValue;
     if (in.type != kI8Codes && !gemv_can_fuse(in.x, in.type, in.ldx, w.K)) return cudaErrorInvalidValue;
     if (out_type != kF16 && out_type != kF32 && (out_type != kI32 || swiglu))
         return cudaErrorInvalidValue;

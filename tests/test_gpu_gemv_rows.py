@@ -2,8 +2,10 @@
 exercise its layouts: W4 activation codes interleaved in shared memory (16-byte halves of
 each 32-code unit grouped per block of 32 units, a row's last block partial), tasks of two
 weight rows (W4 at 3..8 rows, W8 at 5..8: the CTA's rows split in halves, the second one row
-shorter when the count is odd), rows cut into several chunks, and the path that reads
-codes quantised by the separate kernel (K not a multiple of the fused prologue's vector)."""
+shorter when the count is odd), rows cut into several chunks, the balanced mode at one or
+two rows ((row, chunk) tasks dealt round-robin to the warps, int32 sums added in shared
+memory), and the path that reads codes quantised by the separate kernel (K not a multiple
+of the fused prologue's vector)."""
 import numpy as np
 import pytest
 import torch
@@ -26,6 +28,12 @@ CASES = [
     (8, 2560, 9728, 6),
     (8, 2560, 1000, 3),     # W8 unpaired at four rows
     (8, 203, 300, 8),
+    # balanced (row, chunk) tasks at one or two rows, sums added in shared memory
+    (8, 2560, 9728, 1),     # cfg1: whole rows (66 per CTA)
+    (8, 9728, 2560, 1),     # balanced: 18 rows per CTA in one-unit tasks
+    (4, 9728, 2560, 2),     # two-unit tasks
+    (8, 4096, 2560, 2),
+    (4, 8192, 7168, 1),
 ]
 
 
