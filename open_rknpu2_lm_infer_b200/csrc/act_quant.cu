@@ -94,7 +94,9 @@ __device__ __forceinline__ int block_sum(int v, int *red) {
 template <typename T>
 __global__ void __launch_bounds__(kThreads) act_quant_vec_kernel(
     const T *__restrict__ x, long long ldx, int K, int Kp, int round_mode,
-    int8_t *__restrict__ codes, float *__restrict__ scales, int32_t *__restrict__ rowsums) {
+    int8_t *__restrict__ codes, float *__restrict__ scales, int32_t *__restrict__ rowsums,
+    int early) {
+    if (early) asm volatile("griddepcontrol.launch_dependents;");
     constexpr int V = Vec<T>::N;
     __shared__ float redf[32];
     __shared__ int redi[32];
@@ -161,18 +163,22 @@ __global__ void __launch_bounds__(kThreads) act_quant_vec_kernel(
         if (rowsums) rowsums[m] = sum;
     }
     // Let a dependent kernel launched with programmatic stream serialization (the GEMM /
-    // GEMV) launch once every row's CTA got here; it waits (griddepcontrol.wait) before
-    // reading what this kernel wrote.  Triggering at the end rather than the start keeps
-    // the dependent's CTAs (a GEMM CTA holds most of an SM) from crowding out the rows
-    // still to be quantised.
-    asm volatile("griddepcontrol.launch_dependents;");
+    // GEMV) launch; it waits (griddepcontrol.wait) for this grid's completion and memory
+    // before reading what this kernel wrote.  The dependent launches only once every CTA of
+    // this grid has issued the instruction or exited, so no dependent CTA can take an SM a
+    // row still waiting to be scheduled needs.  With `early` (the whole grid resident at
+    // once) it was issued at the start, so the dependent's launch, prologue and first weight
+    // loads overlap the quantisation; larger grids keep it here, at the end.
+    if (!early) asm volatile("griddepcontrol.launch_dependents;");
 }
 
 // Scalar path for any K / alignment (re-reads the row for the second pass).
 template <typename T>
 __global__ void __launch_bounds__(kThreads) act_quant_scalar_kernel(
     const T *__restrict__ x, long long ldx, int K, int Kp, int round_mode,
-    int8_t *__restrict__ codes, float *__restrict__ scales, int32_t *__restrict__ rowsums) {
+    int8_t *__restrict__ codes, float *__restrict__ scales, int32_t *__restrict__ rowsums,
+    int early) {
+    if (early) asm volatile("griddepcontrol.launch_dependents;");
     __shared__ float redf[32];
     __shared__ int redi[32];
     const long long m = blockIdx.x;
@@ -195,7 +201,23 @@ __global__ void __launch_bounds__(kThreads) act_quant_scalar_kernel(
         scales[m] = scale;
         if (rowsums) rowsums[m] = sum;
     }
-    asm volatile("griddepcontrol.launch_dependents;");
+    if (!early) asm volatile("griddepcontrol.launch_dependents;");
+}
+
+// CTAs of `kern` the current device holds at once (0 if unknown); cached per device.
+template <typename K>
+int resident_ctas(K kern, int (&cache)[64]) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    if (cache[dev] == 0) {
+        int per_sm = 0, sms = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, 0) !=
+                cudaSuccess ||
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            return 0;
+        cache[dev] = per_sm * sms > 0 ? per_sm * sms : -1;
+    }
+    return cache[dev] > 0 ? cache[dev] : 0;
 }
 
 template <typename T>
@@ -204,12 +226,18 @@ cudaError_t launch_typed(const T *x, long long ldx, int rows, int K, int Kp, int
     constexpr int V = Vec<T>::N;
     const bool vec = (K % V == 0) && (ldx % V == 0) &&
                      ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
-    if (vec)
+    // A grid no larger than the resident capacity triggers the dependent launch at its start
+    // (see the kernels).
+    static int cap_vec[64] = {0}, cap_scalar[64] = {0};
+    if (vec) {
+        const int early = rows <= resident_ctas(act_quant_vec_kernel<T>, cap_vec) ? 1 : 0;
         act_quant_vec_kernel<T><<<rows, kThreads, 0, stream>>>(x, ldx, K, Kp, round_mode, codes,
-                                                               scales, rowsums);
-    else
+                                                               scales, rowsums, early);
+    } else {
+        const int early = rows <= resident_ctas(act_quant_scalar_kernel<T>, cap_scalar) ? 1 : 0;
         act_quant_scalar_kernel<T><<<rows, kThreads, 0, stream>>>(x, ldx, K, Kp, round_mode,
-                                                                  codes, scales, rowsums);
+                                                                  codes, scales, rowsums, early);
+    }
     return cudaGetLastError();
 }
 
