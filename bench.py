@@ -481,7 +481,38 @@ def decode_measure(backend, torch, dev, args, world):
     hbm = measured_peaks().get("hbm_gbs", 6650.0)
     for l in lins:
         l.close()
-    return {"config": "cfg1 W8A8 K2560 N9728 M1 (8 rotated weight copies, 200 MB > L2)",
+    large = None
+    if world == 1:
+        # the largest decode linear of the cfg3 model, the W8 lm_head 2560 -> 151936 (389 MB):
+        # the same kernel once a layer is long enough to amortise the per-launch ramp
+        kl, nl = 2560, 151936
+        codes_l, scales_l = W.weight_codes(8, kl, nl), W.weight_scales(nl)
+        heads = [backend.load(QuantMatrix(8, kl, nl, codes_l, scales_l)) for _ in range(2)]
+        del codes_l
+        yl = torch.empty((1, nl), dtype=torch.float16, device=dev)
+        xl = torch.from_numpy(W.activations(1, kl, stream=6)).to(dev)
+        for i in range(4):
+            heads[i % 2].run_device(xl, yl, 1, stream=stream)
+        ts = []
+        for _ in range(3):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda._sleep(int(5e7))
+            e0.record()
+            for i in range(8):
+                heads[i % 2].run_device(xl, yl, 1, stream=stream)
+            e1.record()
+            torch.cuda.synchronize(dev)
+            ts.append(e0.elapsed_time(e1) * 1e-3 / 8)
+        backend.check(stream)
+        tl = statistics.median(ts)
+        bl = kl * nl + 4 * nl + 2 * kl + 2 * nl
+        large = {"config": "lm_head W8A8 K2560 N151936 M1 (2 alternating copies, 778 MB)",
+                 "call_us": tl * 1e6, "value": bl / tl / 1e9, "unit": "GB/s",
+                 "frac": bl / tl / 1e9 / hbm}
+        for h in heads:
+            h.close()
+    return {"large_layer": large,
+            "config": "cfg1 W8A8 K2560 N9728 M1 (8 rotated weight copies, 200 MB > L2)",
             "call_us": per_call * 1e6,
             "call_us_alone": alone * 1e6,
             "value_alone": algo / alone / 1e9,
@@ -720,9 +751,50 @@ def run_sweep(args):
                          for layer in layers for lname, bits, k, n, _ in layer)
             emit(f"cfg3 36 layers x (qkv, o, gate/up+SwiGLU, down), {n_w4}/144 linears W4",
                  m, secs, ops, bytes_, launches, {"ms_per_pass": secs * 1e3})
+            if m == 1:
+                # the same decode pass captured once into a CUDA graph and replayed (every
+                # call at one token allocates nothing; the launches' programmatic stream
+                # serialization becomes programmatic edges of the graph)
+                g = torch.cuda.CUDAGraph()
+                cap = torch.cuda.Stream(dev)
+                cap.wait_stream(torch.cuda.current_stream(dev))
+                with torch.cuda.stream(cap):
+                    stream_saved = stream
+                    stream = cap.cuda_stream
+                    chain()  # warm on the capture stream
+                    cap.synchronize()
+                    with torch.cuda.graph(g, stream=cap):
+                        chain()
+                    stream = stream_saved
+                torch.cuda.current_stream(dev).wait_stream(cap)
+                secs_g = time_chain(g.replay, reps=3)
+                emit(f"cfg3 36 layers decode pass as one CUDA graph (replay)", m, secs_g, ops,
+                     bytes_, launches, {"ms_per_pass": secs_g * 1e3})
+                del g
         for layer in layers:
             for *_, lin in layer:
                 lin.close()
+
+    # lm_head: W8 2560 -> 151936 (the vocabulary projection of the Qwen3-4B-shaped model)
+    if want("lmhead"):
+        bits, k, n = 8, 2560, 151936
+        lins = load(bits, k, n, 2)  # 2 x 389 MB: every call streams from HBM
+        for m in (1, 512):
+            x = act(m, k)
+            y = torch.empty((m, n), dtype=torch.float16, device=dev)
+
+            def chain():
+                for lin in lins:
+                    lin.run_device(x, y, m, stream=stream)
+            b0 = backend.launches()
+            secs = time_chain(chain) / len(lins)
+            launches = (backend.launches() - b0) / (7 * len(lins))
+            emit(f"lmhead W8A8 K{k} N{n}", m, secs, 2.0 * m * k * n,
+                 kernel_bytes(bits, k, n, m) + 2 * m * k + 2 * m * n, launches, {"copies": 2})
+            del x, y
+        for lin in lins:
+            lin.close()
+        codes_cache.clear()
 
     clocks = sampler.stop()
     print(json.dumps({"sweep_done": True, "swiglu": "unfused" if args.swiglu_unfused else
