@@ -243,6 +243,30 @@ QLINEAR_API int qlinear_act_quant_device(qlinear_backend *backend, const void *a
                              int K, int8_t *codes_dev, float *scales_dev, int32_t *rowsums_dev,
                              void *stream);
 
+/* Row-parallel (split-K) linear over ranks (no reference counterpart; the reference is
+ * single-device).  A rank holds the weight rows of its K slice (a weights object of K_slice
+ * inputs) and the matching slice of every activation row.  The reference's arithmetic
+ * (src/npu.rs:1099-1117) is kept exactly:
+ *   qlinear_row_amax_device: amax_dev[m] = max |a[m][:]| of this slice (NaN ignored);
+ *   (the caller takes the max over the ranks, e.g. an all-reduce MAX)
+ *   qlinear_run_device_amax: the slice quantised with the scale of the given whole-row max
+ *     (so the codes are those of the whole row), c_type QLINEAR_I32 gives this slice's exact
+ *     int32 partial accumulators (the W4 offset already removed);
+ *   (the caller sums the partial accumulators over the ranks, e.g. an int32 all-reduce SUM)
+ *   qlinear_dequant_device: c[m][n] = (f32(acc[m][n]) * s_a[m]) * s_w[n], s_a the scale of
+ *     row_amax[m], s_w the weights' scales (every rank's slice has the same N and scales).
+ * The result equals the unsplit linear bit for bit.  Asynchronous on `stream`. */
+QLINEAR_API int qlinear_row_amax_device(qlinear_backend *backend, const void *a_dev, int a_type,
+                                        int rows, int K, float *amax_dev, void *stream);
+QLINEAR_API int qlinear_run_device_amax(qlinear_backend *backend, const qlinear_weights *weights,
+                                        const void *a_dev, int a_type, const float *row_amax_dev,
+                                        void *c_dev, int c_type, long long ldc, int rows,
+                                        void *stream);
+QLINEAR_API int qlinear_dequant_device(qlinear_backend *backend, const qlinear_weights *weights,
+                                       const int32_t *acc_dev, long long lda,
+                                       const float *row_amax_dev, void *c_dev, int c_type,
+                                       long long ldc, int rows, void *stream);
+
 /* Column-parallel (split-N) output assembly: src holds `shards` slabs [rows][shard_cols]
  * back to back (the layout an all-gather of per-rank outputs produces), dst is
  * [rows][shards * shard_cols] with dst[m][s * shard_cols + j] = src[s][m][j].  elem_bytes

@@ -82,6 +82,10 @@ SIGNATURES = {
     "qlinear_peer_signal_wait": (_I, [_P, _P, _I, _I, ctypes.c_ulonglong, ctypes.c_ulonglong, _P]),
     "qlinear_run_device": (_I, [_P, _P, _P, _I, _P, _I, ctypes.c_longlong, _I, ctypes.c_uint, _P]),
     "qlinear_run_mlp_device": (_I, [_P, _P, _P, _P, _I, _P, _I, ctypes.c_longlong, _I, _P]),
+    "qlinear_row_amax_device": (_I, [_P, _P, _I, _I, _I, _P, _P]),
+    "qlinear_run_device_amax": (_I, [_P, _P, _P, _I, _P, _P, _I, ctypes.c_longlong, _I, _P]),
+    "qlinear_dequant_device": (_I, [_P, _P, _P, ctypes.c_longlong, _P, _P, _I, ctypes.c_longlong,
+                                    _I, _P]),
     "qlinear_act_quant_device": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _P]),
     "qlinear_run_device_noalloc": (_I, [_P, _P, _I, _P, _I, ctypes.c_longlong, _I, _P]),
     "qlinear_interleave_columns": (_I, [_P, _P, _P, _I, _I, _I, _I, _P]),

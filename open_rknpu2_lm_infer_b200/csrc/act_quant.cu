@@ -95,7 +95,7 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads) act_quant_vec_kernel(
     const T *__restrict__ x, long long ldx, int K, int Kp, int round_mode,
     int8_t *__restrict__ codes, float *__restrict__ scales, int32_t *__restrict__ rowsums,
-    int early) {
+    const float *__restrict__ amax_in, int early) {
     if (early) asm volatile("griddepcontrol.launch_dependents;");
     constexpr int V = Vec<T>::N;
     __shared__ float redf[32];
@@ -125,7 +125,9 @@ __global__ void __launch_bounds__(kThreads) act_quant_vec_kernel(
 #pragma unroll
         for (int e = 0; e < V; e++) amax = fmaxf(amax, fabsf(t[e]));
     }
-    amax = block_max(amax, redf);
+    // amax_in: the row's max |x| given by the caller (the max over every rank's slice of a
+    // K-split row), so the codes are those of the whole row
+    amax = amax_in ? amax_in[m] : block_max(amax, redf);
     float scale, inv;
     a8_row_scale(amax, scale, inv);
 
@@ -177,7 +179,7 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads) act_quant_scalar_kernel(
     const T *__restrict__ x, long long ldx, int K, int Kp, int round_mode,
     int8_t *__restrict__ codes, float *__restrict__ scales, int32_t *__restrict__ rowsums,
-    int early) {
+    const float *__restrict__ amax_in, int early) {
     if (early) asm volatile("griddepcontrol.launch_dependents;");
     __shared__ float redf[32];
     __shared__ int redi[32];
@@ -185,8 +187,12 @@ __global__ void __launch_bounds__(kThreads) act_quant_scalar_kernel(
     const T *xr = x + m * ldx;
     int8_t *cr = codes + m * (long long)Kp;
     float amax = 0.0f;
-    for (int k = threadIdx.x; k < K; k += kThreads) amax = fmaxf(amax, fabsf(to_f32(xr[k])));
-    amax = block_max(amax, redf);
+    if (amax_in) {
+        amax = amax_in[m];
+    } else {
+        for (int k = threadIdx.x; k < K; k += kThreads) amax = fmaxf(amax, fabsf(to_f32(xr[k])));
+        amax = block_max(amax, redf);
+    }
     float scale, inv;
     a8_row_scale(amax, scale, inv);
     int sum = 0;
@@ -222,7 +228,8 @@ int resident_ctas(K kern, int (&cache)[64]) {
 
 template <typename T>
 cudaError_t launch_typed(const T *x, long long ldx, int rows, int K, int Kp, int round_mode,
-                         int8_t *codes, float *scales, int32_t *rowsums, cudaStream_t stream) {
+                         int8_t *codes, float *scales, int32_t *rowsums, cudaStream_t stream,
+                         const float *amax_in) {
     constexpr int V = Vec<T>::N;
     const bool vec = (K % V == 0) && (ldx % V == 0) &&
                      ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
@@ -232,11 +239,12 @@ cudaError_t launch_typed(const T *x, long long ldx, int rows, int K, int Kp, int
     if (vec) {
         const int early = rows <= resident_ctas(act_quant_vec_kernel<T>, cap_vec) ? 1 : 0;
         act_quant_vec_kernel<T><<<rows, kThreads, 0, stream>>>(x, ldx, K, Kp, round_mode, codes,
-                                                               scales, rowsums, early);
+                                                               scales, rowsums, amax_in, early);
     } else {
         const int early = rows <= resident_ctas(act_quant_scalar_kernel<T>, cap_scalar) ? 1 : 0;
         act_quant_scalar_kernel<T><<<rows, kThreads, 0, stream>>>(x, ldx, K, Kp, round_mode,
-                                                                  codes, scales, rowsums, early);
+                                                                  codes, scales, rowsums, amax_in,
+                                                                  early);
     }
     return cudaGetLastError();
 }
@@ -245,13 +253,13 @@ cudaError_t launch_typed(const T *x, long long ldx, int rows, int K, int Kp, int
 
 cudaError_t launch_act_quant(const void *x, int x_type, long long ldx, int rows, int K, int Kp,
                              int round_mode, int8_t *codes, float *scales, int32_t *rowsums,
-                             cudaStream_t stream) {
+                             cudaStream_t stream, const float *amax_in) {
     if (rows <= 0) return cudaSuccess;
     if (x_type == kF16)
         return launch_typed(static_cast<const __half *>(x), ldx, rows, K, Kp, round_mode, codes,
-                            scales, rowsums, stream);
+                            scales, rowsums, stream, amax_in);
     return launch_typed(static_cast<const float *>(x), ldx, rows, K, Kp, round_mode, codes, scales,
-                        rowsums, stream);
+                        rowsums, stream, amax_in);
 }
 
 }  // namespace ql

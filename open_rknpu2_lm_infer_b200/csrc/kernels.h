@@ -44,9 +44,19 @@ struct ActView {
     int rows_cap;          // rows the codes buffer holds (>= rows of the call)
 };
 
+// amax_in (optional, [rows]): the rows' max |x| given by the caller instead of computed here.
 cudaError_t launch_act_quant(const void *x, int x_type, long long ldx, int rows, int K, int Kp,
                              int round_mode, int8_t *codes, float *scales, int32_t *rowsums,
-                             cudaStream_t stream);
+                             cudaStream_t stream, const float *amax_in = nullptr);
+
+// Split-K helpers (split_k.cu).  Row max |x| of x [rows][K] (NaN ignored, like act_quant), and
+// the dequant of int32 accumulators acc [rows][lda] (summed over the K slices):
+// out[m][n] = (f32(acc[m][n]) * s_a[m]) * s_w[n] with s_a the act_quant scale of amax[m].
+cudaError_t launch_row_amax(const void *x, int x_type, long long ldx, int rows, int K, float *amax,
+                            cudaStream_t stream);
+cudaError_t launch_dequant(const int32_t *acc, long long lda, const float *amax,
+                           const float *wscale, int rows, int N, void *out, int out_type,
+                           long long ldc, int num_sms, cudaStream_t stream);
 
 // Weight packing from the QuantMatrix layout int8 [K][N] (device copy) into the device
 // layout above; only columns [n_begin, n_begin + N) of a matrix with n_total columns.

@@ -290,9 +290,11 @@ int next_prof_events(qlinear_backend *b, const std::array<cudaEvent_t, 3> **out)
 
 // outs: where the output goes (this GPU's buffer, plus peers' for the split-N exchange);
 // c_dev = outs.dst[0].
+// amax_in (optional, device [rows]): quantise with these row maxima (a K-split row's max over
+// every rank's slice) instead of each row's own.
 int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_dev, int a_type,
                     const OutputSet &outs, int c_type, long long ldc, int rows, unsigned flags,
-                    cudaStream_t stream) {
+                    cudaStream_t stream, const float *amax_in = nullptr) {
     const WeightView &v = w->view;
     const bool swiglu = (flags & QLINEAR_RUN_SWIGLU) != 0;
     const int width = swiglu ? v.N / 2 : v.N;
@@ -309,7 +311,8 @@ int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_
 
     int st;
     const std::array<cudaEvent_t, 3> *ev = nullptr;
-    if (gemv_fits(rows, v.Kp, v.N, v.bits, swiglu, b->num_sms) && gemv_can_fuse(a_dev, a_type, v.K, v.K)) {
+    if (!amax_in && gemv_fits(rows, v.Kp, v.N, v.bits, swiglu, b->num_sms) &&
+        gemv_can_fuse(a_dev, a_type, v.K, v.K)) {
         // decode: one kernel that quantises the rows itself and streams the weights
         if (b->profiling) {
             if ((st = next_prof_events(b, &ev))) return st;
@@ -331,7 +334,7 @@ int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_
     }
     int8_t *codes = reinterpret_cast<int8_t *>(b->d_ws);
     QL_TRY(launch_act_quant(a_dev, a_type, v.K, rows, v.K, v.Kp, b->round_mode, codes, b->d_ascale,
-                            b->d_rowsum, stream));
+                            b->d_rowsum, stream, amax_in));
     b->launches++;
     if (ev) QL_TRY(cudaEventRecord((*ev)[1], stream));
     struct Stop {  // records the third event on every exit path below
@@ -826,6 +829,38 @@ int qlinear_act_quant_device(qlinear_backend *b, const void *a_dev, int a_type, 
     DeviceGuard guard(b->device);
     QL_TRY(launch_act_quant(a_dev, a_type, K, rows, K, K, b->round_mode, codes_dev, scales_dev,
                             rowsums_dev, static_cast<cudaStream_t>(stream)));
+    b->launches++;
+    return QLINEAR_OK;
+}
+
+int qlinear_row_amax_device(qlinear_backend *b, const void *a_dev, int a_type, int rows, int K,
+                            float *amax_dev, void *stream) {
+    if (!b || !a_dev || !amax_dev || rows < 1 || K < 1 || !valid_io_type(a_type))
+        return QLINEAR_ERR_PARAM;
+    DeviceGuard guard(b->device);
+    QL_TRY(launch_row_amax(a_dev, a_type, K, rows, K, amax_dev, static_cast<cudaStream_t>(stream)));
+    b->launches++;
+    return QLINEAR_OK;
+}
+
+int qlinear_run_device_amax(qlinear_backend *b, const qlinear_weights *w, const void *a_dev,
+                            int a_type, const float *row_amax_dev, void *c_dev, int c_type,
+                            long long ldc, int rows, void *stream) {
+    if (!b || !w || w->backend != b || !row_amax_dev) return QLINEAR_ERR_PARAM;
+    DeviceGuard guard(b->device);
+    return run_device_impl(b, w, a_dev, a_type, single_output(c_dev), c_type, ldc, rows, 0,
+                           static_cast<cudaStream_t>(stream), row_amax_dev);
+}
+
+int qlinear_dequant_device(qlinear_backend *b, const qlinear_weights *w, const int32_t *acc_dev,
+                           long long lda, const float *row_amax_dev, void *c_dev, int c_type,
+                           long long ldc, int rows, void *stream) {
+    if (!b || !w || w->backend != b || !acc_dev || !row_amax_dev || !c_dev || rows < 1 ||
+        !valid_io_type(c_type) || lda < w->view.N || ldc < w->view.N)
+        return QLINEAR_ERR_PARAM;
+    DeviceGuard guard(b->device);
+    QL_TRY(launch_dequant(acc_dev, lda, row_amax_dev, w->view.scales, rows, w->view.N, c_dev,
+                          c_type, ldc, b->num_sms, static_cast<cudaStream_t>(stream)));
     b->launches++;
     return QLINEAR_OK;
 }

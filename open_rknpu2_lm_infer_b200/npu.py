@@ -38,6 +38,17 @@ import numpy as np
 from . import _lib as L
 
 
+def _dtype_code(t) -> int:
+    s = str(getattr(t, "dtype", ""))
+    if "float16" in s:
+        return L.F16
+    if "float32" in s:
+        return L.F32
+    if "int32" in s:
+        return L.I32
+    raise TypeError(s)
+
+
 class NpuError(RuntimeError):
     def __init__(self, op: str, rc: int):
         self.op, self.rc = op, rc
@@ -243,6 +254,11 @@ class Backend:
             self.raw, gate_up._raw, down._raw, _ptr(a), code(a), _ptr(out), code(out),
             down.n() if ldc is None else ldc, rows, stream), "MLP device run")
 
+    def row_amax_device(self, a, rows: int, k: int, amax, stream=None) -> None:
+        """amax[m] = max |a[m][:k]| (device buffers; NaN ignored like Rust's f32::max)."""
+        _check(self._lib.qlinear_row_amax_device(self.raw, _ptr(a), _dtype_code(a), rows, k,
+                                                 _ptr(amax), stream), "row amax")
+
     def act_quant_device(self, a, rows: int, k: int, codes, scales, rowsums=None,
                          stream=None) -> None:
         """Activation quantisation alone (device buffers); exports the int8 codes."""
@@ -369,6 +385,20 @@ class Linear:
         _check(self._lib.qlinear_run_device(
             self._backend.raw, self._raw, _ptr(a), a_type, _ptr(out), c_type, ldc, rows,
             L.RUN_SWIGLU if swiglu else 0, stream), f"W{self.bits} device run")
+
+    def run_device_amax(self, a, row_amax, out, rows: int, stream=None) -> None:
+        """This K slice of a split-K linear: `a` [rows][K_slice] quantised with the scale of
+        the given whole-row maxima `row_amax` [rows]; `out` int32 receives the exact partial
+        accumulators (fp16/f32: this slice's dequantised partial)."""
+        _check(self._lib.qlinear_run_device_amax(
+            self._backend.raw, self._raw, _ptr(a), _dtype_code(a), _ptr(row_amax), _ptr(out),
+            _dtype_code(out), self._n, rows, stream), f"W{self.bits} split-K run")
+
+    def dequant_device(self, acc, row_amax, out, rows: int, stream=None) -> None:
+        """out = (f32(acc) * s_a) * s_w for int32 accumulators summed over the K slices."""
+        _check(self._lib.qlinear_dequant_device(
+            self._backend.raw, self._raw, _ptr(acc), self._n, _ptr(row_amax), _ptr(out),
+            _dtype_code(out), self._n, rows, stream), "dequant")
 
     def run_device_scatter(self, a, outs, out_type: int, ldc: int, col_offset: int, rows: int,
                            swiglu: bool = False, stream=None) -> None:

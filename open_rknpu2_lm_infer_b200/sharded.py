@@ -15,6 +15,9 @@ single-GPU run.  Two ways to put the [M][N] output together on every rank:
   signal array and waits for all of them (``qlinear_peer_signal_wait``), so the output is
   complete on every rank.  No gather, no assembly pass, no collective per call.
 
+``ShardedMLP`` splits a whole MLP block instead (gate/up columns and down rows together:
+no gather of the middle, an exact all-reduce of int32 partial accumulators).
+
 The reference is single-device; this has no counterpart there.
 """
 from __future__ import annotations
@@ -168,3 +171,80 @@ class ShardedLinear:
         self.backend.interleave_columns(gathered, out, self.world, rows, self.ns,
                                         out.element_size(), stream=stream)
         del torch
+
+
+def mlp_shard_matrices(gate_up, down, world: int, rank: int):
+    """Rank `rank`'s pieces of an MLP block split over `world` ranks: the gate/up matrix
+    (gate columns [0, h), up [h, 2h), src/model/checkpoint.rs:392-423) keeps the gate and up
+    columns [lo, hi) of the middle width h -- so SwiGLU stays local -- and the down matrix
+    (K = h) keeps its rows [lo, hi), a K slice.  Returns two QuantMatrix objects."""
+    from .npu import QuantMatrix
+    h = gate_up.n // 2
+    if gate_up.n % 2 or down.k != h:
+        raise ValueError("gate/up must have 2h columns and down h rows")
+    lo, hi = shard_bounds(h, world, rank)
+    gu = np.asarray(gate_up.codes).reshape(gate_up.k, gate_up.n)
+    gsc = np.asarray(gate_up.scales).reshape(-1)
+    codes = np.ascontiguousarray(np.concatenate([gu[:, lo:hi], gu[:, h + lo:h + hi]], axis=1))
+    scales = np.ascontiguousarray(np.concatenate([gsc[lo:hi], gsc[h + lo:h + hi]]))
+    dn = np.asarray(down.codes).reshape(down.k, down.n)
+    return (QuantMatrix(gate_up.bits, gate_up.k, 2 * (hi - lo), codes, scales),
+            QuantMatrix(down.bits, hi - lo, down.n, np.ascontiguousarray(dn[lo:hi]),
+                        np.asarray(down.scales)))
+
+
+class ShardedMLP:
+    """One rank's share of an MLP block (gate/up + SwiGLU -> down, src/model/dense.rs:499-530)
+    split over the ranks of a torch.distributed group without gathering the middle: the
+    gate/up columns and the down rows are split together (``mlp_shard_matrices``), so each
+    rank forms its slice of the middle locally; the down projection is then a K split whose
+    whole-row activation scale comes from an all-reduce MAX of the slices' row maxima (M
+    floats) and whose int32 partial accumulators are summed exactly by an all-reduce SUM
+    (M x hidden int32) before one dequant.  The output on every rank is bit-identical to
+    ``qlinear_run_mlp_device`` on one GPU (the same f32 middle, codes and accumulators)."""
+
+    def __init__(self, backend, gate_up, down, group=None):
+        import torch.distributed as dist
+        self.backend = backend
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        gu, dn = mlp_shard_matrices(gate_up, down, self.world, self.rank)
+        self.hs, self.hidden = gu.n // 2, dn.n
+        self.gate_up = backend.load(gu)
+        self.down = backend.load(dn)
+        self._bufs = {}
+
+    def _buf(self, key, shape, dtype, device):
+        import torch
+        b = self._bufs.get(key)
+        if b is None or tuple(b.shape) != tuple(shape) or b.dtype != dtype:
+            b = torch.empty(shape, dtype=dtype, device=device)
+            self._bufs[key] = b
+        return b
+
+    def run_device(self, a, out, rows: int, stream=None) -> None:
+        """a [rows][hidden] (fp16/f32, replicated); out [rows][hidden] fp16 or f32.  `stream`
+        must be the current torch stream's handle (or None for it): the collectives are
+        ordered after the kernels through it."""
+        import torch
+        import torch.distributed as dist
+        if stream is None:
+            stream = torch.cuda.current_stream(a.device).cuda_stream
+        dev = a.device
+        mid = self._buf("mid", (rows, self.hs), torch.float32, dev)
+        amax = self._buf("amax", (rows,), torch.float32, dev)
+        acc = self._buf("acc", (rows, self.hidden), torch.int32, dev)
+        self.gate_up.run_device(a, mid, rows, swiglu=True, stream=stream)
+        self.backend.row_amax_device(mid, rows, self.hs, amax, stream=stream)
+        if self.world > 1:
+            dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=self.group)
+        self.down.run_device_amax(mid, amax, acc, rows, stream=stream)
+        if self.world > 1:
+            dist.all_reduce(acc, op=dist.ReduceOp.SUM, group=self.group)
+        self.down.dequant_device(acc, amax, out, rows, stream=stream)
+
+    def close(self) -> None:
+        self.gate_up.close()
+        self.down.close()
+        self._bufs = {}

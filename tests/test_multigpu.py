@@ -1,6 +1,8 @@
 """Split-N on 2+ GPUs: the output assembled after an NCCL all-gather, and the output the
 kernels' epilogues store straight into every rank's exchange buffer (fused exchange over
-NVLink peer memory), both equal the single-GPU output bitwise.  Runs as torchrun child
+NVLink peer memory), both equal the single-GPU output bitwise; and the split-K MLP block
+(ShardedMLP: NCCL all-reduces of row maxima and int32 accumulators) equals the single-GPU
+block bitwise.  Runs as torchrun child
 processes; skipped when fewer than 2 GPUs are visible."""
 import os
 import subprocess
@@ -48,6 +50,26 @@ for bits, k, n, rows in [(4, 2560, 4096, 300), (8, 4096, 2048, 3), (4, 8192, 286
             assert torch.equal(got, want_t), (rank, "fused", dtype, bits, k, n, rows)
         fx.close()
     sh.linear.close(); full.close()
+# split-K MLP: gate/up columns and down rows split together, all-reduces of the row maxima
+# and the int32 partial accumulators; equal to the single-GPU block bit for bit
+from open_rknpu2_lm_infer_b200.sharded import ShardedMLP
+hidden, h = 2560, 9728
+gate_up = QuantMatrix(4, hidden, 2 * h, W.weight_codes(4, hidden, 2 * h, stream=90),
+                      W.weight_scales(2 * h, stream=90))
+down = QuantMatrix(8, h, hidden, W.weight_codes(8, h, hidden, stream=91),
+                   W.weight_scales(hidden, stream=91))
+gu_full, dn_full = b.load(gate_up), b.load(down)
+mlp = ShardedMLP(b, gate_up, down)
+for rows in (1, 300):
+    x = torch.from_numpy(W.activations(rows, hidden, stream=92)).cuda()
+    want = torch.empty((rows, hidden), dtype=torch.float16, device="cuda")
+    b.run_mlp_device(gu_full, dn_full, x, want, rows)
+    for _ in range(2):
+        got = torch.empty((rows, hidden), dtype=torch.float16, device="cuda")
+        mlp.run_device(x, got, rows)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want), (rank, "split-K MLP", rows)
+mlp.close(); gu_full.close(); dn_full.close()
 b.check()
 dist.barrier()
 dist.destroy_process_group()
