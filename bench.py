@@ -79,6 +79,10 @@ def parse():
                     help="prefill SwiGLU as GEMM -> f32 workspace -> SwiGLU pass (comparison)")
     ap.add_argument("--stream-k", action="store_true",
                     help="let the GEMM choose its stream-K schedule (QLINEAR_BACKEND_GEMM_STREAM_K)")
+    ap.add_argument("--mlp", action="store_true",
+                    help="time the cfg2 MLP block instead: one GPU qlinear_run_mlp_device, N GPUs "
+                         "the split-K ShardedMLP")
+    ap.add_argument("--mlp-rows", type=int, default=512)
     return ap.parse_args()
 
 
@@ -583,6 +587,77 @@ def e2e_measure(backend, lin, torch, dist, dev, args, world, m, k, n, ns, x_host
                    "qlinear_interleave_columns -> D2H f32"}
 
 
+def run_mlp(args, rank, world, local_rank):
+    """--mlp: the cfg2 MLP block (W4 gate/up 2560 -> 2 x 9728 + SwiGLU -> f32 middle -> W8
+    down 9728 -> 2560) at --mlp-rows tokens.  One GPU: qlinear_run_mlp_device; N GPUs: the
+    split-K ShardedMLP (gate/up columns and down rows split together, NCCL all-reduces of the
+    row maxima and the int32 partial accumulators).  TOPS of the whole block; device time per
+    step with CUDA events (GPU held while the host enqueues; L2 flushed between steps outside
+    the timed region), max over ranks.  Strong scaling."""
+    import torch
+    import torch.distributed as dist
+    from open_rknpu2_lm_infer_b200 import Backend, QuantMatrix
+    from open_rknpu2_lm_infer_b200 import workloads as W
+    from open_rknpu2_lm_infer_b200.sharded import ShardedMLP
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    hidden, h, m = 2560, 9728, args.mlp_rows
+    gate_up = QuantMatrix(4, hidden, 2 * h, W.weight_codes(4, hidden, 2 * h, stream=90),
+                          W.weight_scales(2 * h, stream=90))
+    down = QuantMatrix(8, h, hidden, W.weight_codes(8, h, hidden, stream=91),
+                       W.weight_scales(hidden, stream=91))
+    backend = Backend(device=local_rank)
+    x = torch.from_numpy(W.activations(m, hidden, stream=92)).to(dev)
+    y = torch.empty((m, hidden), dtype=torch.float16, device=dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    if world > 1:
+        mlp = ShardedMLP(backend, gate_up, down)
+        step = lambda: mlp.run_device(x, y, m, stream=stream)  # noqa: E731
+    else:
+        gu, dn = backend.load(gate_up), backend.load(down)
+        step = lambda: backend.run_mlp_device(gu, dn, x, y, m, stream=stream)  # noqa: E731
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    ev = []
+    torch.cuda._sleep(int(2e8))
+    for _ in range(args.steps):
+        flush.zero_()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step()
+        e1.record()
+        ev.append((e0, e1))
+    torch.cuda.synchronize(dev)
+    backend.check(stream)
+    t = torch.tensor([sum(a.elapsed_time(b) for a, b in ev) * 1e-3 / args.steps],
+                     dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    per = t.item()
+    ops = 2.0 * m * hidden * 2 * h + 2.0 * m * h * hidden
+    if rank == 0:
+        print(json.dumps({
+            "metric": "cfg2 MLP block TOPS (W4 gate/up + SwiGLU, W8 down)", "value": ops / per / 1e12,
+            "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": per * 1e3, "higher_is_better": True, "scaling": "strong",
+            "dtype": "int8", "data": "synthetic",
+            "config": {"workload": f"cfg2 MLP block M={m}", "M": m, "hidden": hidden,
+                       "intermediate": h,
+                       "parallelism": "one GPU" if world == 1 else
+                       f"split-K x{world} (gate/up columns + down rows, all-reduce of row "
+                       "maxima and int32 accumulators)",
+                       "l2": "flushed between timed steps, outside the timed region"}}),
+            flush=True)
+    if world > 1:
+        mlp.close()
+    backend.close()
+
+
 def run_sweep(args):
     """--sweep: every named shape on one GPU, one JSON line each.
 
@@ -828,6 +903,9 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
+        if args.mlp:
+            run_mlp(args, rank, world, local_rank)
+            return
         run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
