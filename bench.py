@@ -3,6 +3,8 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload cfg4|cfg0|cfg1|cfg4_m8192] [--exchange fused|gather]
+    python bench.py --sweep [--sweep-cases cfg0,cfg1,...]   # every named shape, one GPU
+    python bench.py --mlp [--mlp-rows M] [--gpus N]           # the cfg2 MLP block
 
 Headline workload (default ``cfg4``): the W4A8 linear K=8192, N=28672 at M=512 tokens,
 split column-parallel over N GPUs (each rank owns N/g output channels); every rank ends
@@ -15,7 +17,8 @@ events, max over ranks), inputs resident in HBM, L2 flushed between timed steps 
 256 MiB write outside the timed region.  Scaling is strong (the layer is fixed).
 
 The line also carries: the decode half of the metric (W8A8 K=2560 N=9728 at M=1, GB/s,
-weights rotated through 8 copies so they come from HBM); the roofline of the dominant
+weights rotated through 8 copies so they come from HBM; at N=1 also the same kernel on the
+389 MB W8 lm_head 2560 -> 151936); the roofline of the dominant
 kernel; the CPU baseline (the C oracle, a bounded row sample, all host threads; rank 0,
 N=1); ``e2e`` through the reference-facing C-ABI call with host f32 buffers
 (qlinear_run_f32 at N=1; H2D -> run with the exchange -> D2H at N>1); SM clocks sampled
