@@ -243,15 +243,8 @@ class Backend:
         """The MLP block of src/model/dense.rs:499-530 on device buffers: out = down(silu(g) *
         u), [g | u] = gate_up(a), with the reference's f32 middle; one fused launch for a
         single row (qlinear_run_mlp_device)."""
-        def code(t):
-            s = str(getattr(t, "dtype", ""))
-            if "float16" in s:
-                return L.F16
-            if "float32" in s:
-                return L.F32
-            raise TypeError(s)
         _check(self._lib.qlinear_run_mlp_device(
-            self.raw, gate_up._raw, down._raw, _ptr(a), code(a), _ptr(out), code(out),
+            self.raw, gate_up._raw, down._raw, _ptr(a), _dtype_code(a), _ptr(out), _dtype_code(out),
             down.n() if ldc is None else ldc, rows, stream), "MLP device run")
 
     def row_amax_device(self, a, rows: int, k: int, amax, stream=None) -> None:
@@ -368,17 +361,8 @@ class Linear:
         """Device-resident call: `a` [rows][K] fp16/f32 and `out` [rows][ldc] (fp16, f32 or
         int32 accumulators) are device buffers (torch tensors or raw pointers); async on
         `stream` (a cudaStream_t value; None = legacy default stream)."""
-        def dtype_code(t):
-            s = str(getattr(t, "dtype", ""))
-            if "float16" in s:
-                return L.F16
-            if "float32" in s:
-                return L.F32
-            if "int32" in s:
-                return L.I32
-            raise TypeError(s)
-        a_type = dtype_code(a)
-        c_type = dtype_code(out) if out_type is None else out_type
+        a_type = _dtype_code(a)
+        c_type = _dtype_code(out) if out_type is None else out_type
         width = self._n // 2 if swiglu else self._n
         if ldc is None:
             ldc = width
