@@ -73,6 +73,8 @@ def parse():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the oracle check of the timed step's output (profiling runs)")
     ap.add_argument("--sweep", action="store_true",
                     help="one GPU: one JSON line per named shape (cfg0-cfg4 and their M sweeps) "
                          "instead of the headline line")
@@ -185,30 +187,79 @@ def cpu_info():
     return os.cpu_count(), model
 
 
-def oracle_sample(bits, k, n, m_total, cpu_seconds, seed_stream=0, max_rows=None):
-    """Time the C oracle (all host threads) on a row sample sized to ~cpu_seconds.
-    Returns (ops_per_s, rows, seconds, threads)."""
+def spread_rows(m_total, rows):
+    """`rows` row indices spread evenly over [0, m_total): they cross every token tile and
+    the last (tail) tiles of the GEMM's schedule, not only the first rows."""
+    rows = max(1, min(int(rows), m_total))
+    return np.unique(np.linspace(0, m_total - 1, rows).round().astype(np.int64))
+
+
+def oracle_sample(bits, k, n, m_total, cpu_seconds, max_rows=None, threads=None, repeats=3):
+    """Time the C oracle on a row sample sized to ~cpu_seconds per run (all host threads
+    unless `threads` is given; the median of `repeats` runs).  The sample's rows are spread over the batch, and the oracle's
+    output for them is returned, so that the caller can compare the timed GPU step with it.
+    Returns (ops_per_s, row indices, seconds, threads, y f32 [rows][n])."""
     from oracle import oracle as O
     from open_rknpu2_lm_infer_b200 import workloads as W
     O.build()
     co = O.COracle()
+    if threads is not None:
+        co.set_threads(threads)
     threads = co.max_threads()
     w = W.weight_codes(bits, k, n)
     sw = W.weight_scales(n)
-    x = W.activations(m_total if max_rows is None else min(m_total, max_rows), k)
+    x = W.activations(m_total, k)
     # probe with one row (warm), then size the sample
     co.linear(w, sw, x[:1])
     t0 = time.perf_counter()
     co.linear(w, sw, x[:1])
     t1 = time.perf_counter() - t0
-    rows = int(max(1, min(x.shape[0], cpu_seconds / max(t1, 1e-6))))
-    t0 = time.perf_counter()
-    co.linear(w, sw, x[:rows])
-    dt = time.perf_counter() - t0
-    return 2.0 * rows * k * n / dt, rows, dt, threads
+    rows = int(max(1, min(m_total, cpu_seconds / max(t1, 1e-6))))
+    if max_rows is not None:
+        rows = min(rows, max_rows)
+    idx = spread_rows(m_total, rows)
+    xs = np.ascontiguousarray(x[idx])
+    y, runs = None, []
+    for _ in range(max(1, repeats)):
+        t0 = time.perf_counter()
+        out = co.linear(w, sw, xs)
+        runs.append(time.perf_counter() - t0)
+        y = out if y is None else y
+    dt = statistics.median(runs)
+    return 2.0 * len(idx) * k * n / dt, idx, dt, threads, y
+
+
+def parity_record(y_gpu_rows, y_oracle, idx):
+    """Bit-exact comparison of the GPU's fp16 rows with f16(oracle f32) (the oracle's f32
+    value rounded once to nearest-even: the same single rounding the epilogue does)."""
+    want = y_oracle.astype(np.float16)
+    got = np.asarray(y_gpu_rows, dtype=np.float16)
+    bad = got.view(np.uint16) != want.view(np.uint16)
+    rec = {"rows_checked": int(len(idx)), "elements_checked": int(want.size),
+           "mismatches": int(np.count_nonzero(bad)),
+           "against": "f16(C oracle f32), bit-exact; rows spread over the batch",
+           "rows": f"{int(idx[0])}..{int(idx[-1])} ({len(idx)} rows)"}
+    if rec["mismatches"]:
+        r, c = np.argwhere(bad)[0]
+        rec["first_mismatch"] = {"row": int(idx[r]), "col": int(c),
+                                 "got": float(got[r, c]), "want": float(want[r, c])}
+    return rec
 
 
 # ----------------------------------------------------------------------------- arms
+def workload_config(args, world):
+    """The `config` object of the JSON line; both arms print the same one."""
+    bits, k, n, m, desc = WORKLOADS[args.workload]
+    fused = args.exchange == "fused"
+    return {"workload": desc, "M": m, "K": k, "N": n, "bits": bits,
+            "parallelism": f"split-N x{world}" + (
+                "" if world == 1 else
+                " + output exchange fused into the kernels (NVLink peer stores)"
+                if fused else " + NCCL all-gather"),
+            "l2": "flushed (256 MiB write) between timed steps, outside the timed region",
+            "inputs": "fp16 N(0,1) with 1% x20 outlier channels, seed 42"}
+
+
 def run_reference(args, rank, world):
     """--impl reference: the reference's CPU implementation of the path (oracle port)."""
     if rank != 0:
@@ -239,14 +290,15 @@ def run_reference(args, rank, world):
     dt = sum(times) / len(times)
     tops = 2.0 * rows * k * n / dt / 1e12
     cores, model = cpu_info()
-    sample = f"{rows} of {m} rows per step ({desc}), C oracle, {threads} OpenMP threads, {model}"
+    sample = (f"{rows} of {m} rows per step ({desc}), C oracle, {threads} OpenMP threads "
+              f"(nproc {cores}), {model}")
     line = {
         "impl": "reference", "metric": "W4A8 linear TOPS (M=512) & decode GB/s (M=1), % of roofline, at 1/2/4/8 B200",
         "value": tops, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dt * 1e3 * m / rows,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "int8", "data": "synthetic",
-        "config": {"workload": desc, "M": m, "K": k, "N": n, "bits": bits},
+        "config": workload_config(args, world),
         "cpu_baseline": {"value": tops, "unit": "TOPS", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": tops, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -363,6 +415,11 @@ def run_ours(args, rank, world, local_rank):
     backend.profile(False)
     quant_ms, main_ms, calls = backend.profile_collect()
     backend.check(stream)
+    # the timed step's output, kept for the parity check against the oracle (rank 0)
+    y_check = None
+    if rank == 0 and not args.no_parity:
+        src = y_local if world == 1 else (sharded.output[:m] if fused else y_full)
+        y_check = src.cpu().numpy()
     step_s = sum(a.elapsed_time(b) for a, b in times) * 1e-3
     t = torch.tensor([step_s, main_ms * 1e-3, quant_ms * 1e-3], dtype=torch.float64, device=dev)
     if world > 1:
@@ -392,13 +449,7 @@ def run_ours(args, rank, world, local_rank):
         "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": mean_step * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": desc, "M": m, "K": k, "N": n, "bits": bits,
-                   "parallelism": f"split-N x{world}" + (
-                       "" if world == 1 else
-                       " + output exchange fused into the kernels (NVLink peer stores)"
-                       if fused else " + NCCL all-gather"),
-                   "l2": "flushed (256 MiB write) between timed steps, outside the timed region",
-                   "inputs": "fp16 N(0,1) with 1% x20 outlier channels, seed 42"},
+        "config": workload_config(args, world),
         "roofline": roofline,
         "gpu_launches": int(launches_timed),
         "clocks": clocks,
@@ -423,21 +474,37 @@ def run_ours(args, rank, world, local_rank):
         line["e2e"] = e2e_measure(backend, lin, torch, dist, dev, args, world, m, k, n, ns,
                                   x_host, sharded)
 
-    if rank == 0 and world == 1 and not args.no_cpu:
-        ops_s, rows, dt, threads = oracle_sample(bits, k, n, m, args.cpu_seconds)
-        cores, model = cpu_info()
-        line["cpu_baseline"] = {
-            "value": ops_s / 1e12, "unit": "TOPS", "cores": threads, "kind": "port",
-            "sample": f"{rows} of {m} rows of {desc}: C oracle (oracle/qlinear_ref.c, OpenMP "
-                      f"{threads} threads, {model}), {dt:.1f} s"}
     line["gpu_launches"] = int(launches_timed)
-    if rank == 0:
-        print(json.dumps(line), flush=True)
     if sharded is not None:
         sharded.close()  # collective: unmaps the peers' buffers, frees this rank's
     else:
         lin.close()
     backend.close()
+    if rank != 0:
+        return
+    # CPU legs after every collective of this arm (rank 0 only): the oracle's rows both time
+    # the CPU baseline (N=1) and check the timed step's output
+    cores, model = cpu_info()
+    oracle_y = None
+    if world == 1 and not args.no_cpu:
+        ops_s, idx, dt, threads, oracle_y = oracle_sample(bits, k, n, m, args.cpu_seconds / 3)
+        ops_1, idx1, dt1, _, _ = oracle_sample(bits, k, n, m, args.cpu_seconds / 4,
+                                               threads=1, repeats=3)
+        line["cpu_baseline"] = {
+            "value": ops_s / 1e12, "unit": "TOPS", "cores": threads, "kind": "port",
+            "sample": f"{len(idx)} of {m} rows of {desc} (spread over the batch): C oracle "
+                      f"(oracle/qlinear_ref.c), OpenMP {threads} threads, median of 3 runs of "
+                      f"{dt:.2f} s",
+            "host": {"nproc": cores, "cpu_model": model},
+            "single_thread": {"value": ops_1 / 1e12, "unit": "TOPS", "cores": 1,
+                              "sample": f"{len(idx1)} of {m} rows, median of 3 runs of "
+                                        f"{dt1:.2f} s"}}
+    if y_check is not None:
+        if oracle_y is None:
+            _, idx, _, _, oracle_y = oracle_sample(bits, k, n, m, 6.0, max_rows=1024,
+                                                   repeats=1)
+        line["parity"] = parity_record(y_check[idx], oracle_y, idx)
+    print(json.dumps(line), flush=True)
 
 
 def decode_measure(backend, torch, dev, args, world):
@@ -798,37 +865,41 @@ def run_sweep(args):
         del gus, downs
         codes_cache.clear()
 
-    # cfg3: the linears of 36 decoder layers (W4/W8 per linear from the seeded draw)
+    # cfg3: the linears of 36 decoder layers (W4/W8 per linear from the seeded draw), loaded
+    # and called through DenseLayerLinears the way the reference's dense model does it
     if want("cfg3"):
-        draw = W.layer_bits()
-        layers = []
-        for li, row in enumerate(draw):
-            layer = []
-            for (lname, k, n), bits in zip(W.QWEN3_4B_LAYER, row):
-                layer.append((lname, bits, k, n, load(bits, k, n, 1)[0]))
-            layers.append(layer)
-        n_w4 = sum(b == 4 for row in draw for b in row)
+        from open_rknpu2_lm_infer_b200.layers import DenseLayerLinears
+        Q = W.QWEN3_4B
+        mbits = W.cfg3_module_bits(Q["layers"])
+        ck = W.SyntheticCheckpoint(mbits, share_by_shape=True)
+        layers = [DenseLayerLinears.load(backend, ck, f"model.layers.{i}.", Q["hidden"],
+                                         Q["q_heads"], Q["kv_heads"], Q["head_dim"],
+                                         Q["intermediate"]) for i in range(Q["layers"])]
+        n_w4 = sum(lin.bits == 4 for layer in layers for _, lin, _ in layer.linears())
+        n_lin = sum(1 for layer in layers for _ in layer.linears())
         for m in (1, 512):
             xs = {k: act(m, k, stream_id=k) for k in (2560, 4096)}
             outs = {n: torch.empty((m, n), dtype=torch.float16, device=dev) for n in (6144, 2560)}
 
             def chain():
                 for layer in layers:
-                    lins = {lname: lin for lname, _, _, _, lin in layer}
-                    lins["qkv"].run_device(xs[2560], outs[6144], m, stream=stream)
-                    lins["o"].run_device(xs[4096], outs[2560], m, stream=stream)
-                    # the MLP block: gate/up + SwiGLU -> f32 middle -> down
-                    backend.run_mlp_device(lins["gate_up"], lins["down"], xs[2560], outs[2560], m,
-                                           stream=stream)
+                    layer.qkv_device(xs[2560], outs[6144], m, stream=stream)
+                    layer.o_device(xs[4096], outs[2560], m, stream=stream)
+                    # the MLP: gate/up + SwiGLU -> f32 middle -> down
+                    layer.mlp_device(xs[2560], outs[2560], m, stream=stream)
             b0 = backend.launches()
             secs = time_chain(chain, reps=3)
             launches = (backend.launches() - b0) / 5
-            ops = sum(2.0 * m * k * n for layer in layers for _, _, k, n, _ in layer)
-            bytes_ = sum(kernel_bytes(bits, k, n, m) + 2 * m * k
-                         + 2 * m * (n // 2 if lname == "gate_up" else n)
-                         for layer in layers for lname, bits, k, n, _ in layer)
-            emit(f"cfg3 36 layers x (qkv, o, gate/up+SwiGLU, down), {n_w4}/144 linears W4",
-                 m, secs, ops, bytes_, launches, {"ms_per_pass": secs * 1e3})
+            ops = bytes_ = 0.0
+            for layer in layers:
+                for role, lin, _ in layer.linears():
+                    k, n = lin.k(), lin.n()
+                    ops += 2.0 * m * k * n
+                    bytes_ += kernel_bytes(lin.bits, k, n, m) + 2 * m * k + 2 * m * (
+                        n // 2 if role == "gate_up" else n)
+            emit(f"cfg3 36 layers x (qkv, o, gate/up+SwiGLU, down) through DenseLayerLinears, "
+                 f"{n_w4}/{n_lin} linears W4", m, secs, ops, bytes_, launches,
+                 {"ms_per_pass": secs * 1e3})
             if m == 1:
                 # the same decode pass captured once into a CUDA graph and replayed (every
                 # call at one token allocates nothing; the launches' programmatic stream
@@ -850,28 +921,31 @@ def run_sweep(args):
                      bytes_, launches, {"ms_per_pass": secs_g * 1e3})
                 del g
         for layer in layers:
-            for *_, lin in layer:
-                lin.close()
+            layer.close()
 
     # lm_head: W8 2560 -> 151936 (the vocabulary projection of the Qwen3-4B-shaped model)
     if want("lmhead"):
+        from open_rknpu2_lm_infer_b200.layers import OutputHead
         bits, k, n = 8, 2560, 151936
-        lins = load(bits, k, n, 2)  # 2 x 389 MB: every call streams from HBM
+        ckh = W.SyntheticCheckpoint({"lm_head": 8})
+        # 2 x 389 MB: every call streams from HBM
+        heads = [OutputHead.quantized(backend, ckh, n, k) for _ in range(2)]
+        lins = [h.linear for h in heads]
         for m in (1, 512):
             x = act(m, k)
             y = torch.empty((m, n), dtype=torch.float16, device=dev)
 
             def chain():
-                for lin in lins:
-                    lin.run_device(x, y, m, stream=stream)
+                for head in heads:
+                    head.run_device(x, y, m, stream=stream)
             b0 = backend.launches()
             secs = time_chain(chain) / len(lins)
             launches = (backend.launches() - b0) / (7 * len(lins))
-            emit(f"lmhead W8A8 K{k} N{n}", m, secs, 2.0 * m * k * n,
+            emit(f"lmhead W8A8 K{k} N{n} (OutputHead)", m, secs, 2.0 * m * k * n,
                  kernel_bytes(bits, k, n, m) + 2 * m * k + 2 * m * n, launches, {"copies": 2})
             del x, y
-        for lin in lins:
-            lin.close()
+        for head in heads:
+            head.close()
         codes_cache.clear()
 
     clocks = sampler.stop()

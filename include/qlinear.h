@@ -267,6 +267,17 @@ QLINEAR_API int qlinear_dequant_device(qlinear_backend *backend, const qlinear_w
                                        const float *row_amax_dev, void *c_dev, int c_type,
                                        long long ldc, int rows, void *stream);
 
+/* SiLU-gated product of a gate/up projection output held on the device, replacing the CPU
+ * fallback of src/model/dense.rs:509-523 (`gate_up.run` into [rows][2f], then `Cpu::swiglu`,
+ * src/model/cpu.rs:327-351), which the reference takes when gate and up have different bit
+ * widths and so are two matrices: y_dev f32 [rows][N] (gate columns [0, N/2), up [N/2, N)),
+ * c_dev [rows][ldc] of c_type (QLINEAR_F16 or QLINEAR_F32), ldc >= N/2,
+ * c[m][j] = silu(y[m][j]) * y[m][N/2 + j] with the same f32 arithmetic as the fused SwiGLU
+ * epilogues.  Asynchronous on `stream`. */
+QLINEAR_API int qlinear_swiglu_device(qlinear_backend *backend, const float *y_dev, int rows,
+                                      int N, void *c_dev, int c_type, long long ldc,
+                                      void *stream);
+
 /* Column-parallel (split-N) output assembly: src holds `shards` slabs [rows][shard_cols]
  * back to back (the layout an all-gather of per-rank outputs produces), dst is
  * [rows][shards * shard_cols] with dst[m][s * shard_cols + j] = src[s][m][j].  elem_bytes
@@ -296,8 +307,9 @@ QLINEAR_API int qlinear_backend_profile_collect(qlinear_backend *backend, double
  *   Limits: rows <= QLINEAR_NOALLOC_MAX_ROWS and K (rounded up to 128) <= QLINEAR_NOALLOC_MAX_K;
  *   larger requests return QLINEAR_ERR_LIMIT without launching anything.
  *   The first call on a device looks the scratch up (cudaGetSymbolAddress, which may load
- *   the library's device code on that device); make that first call before any stream
- *   capture.
+ *   the library's device code on that device) and keeps its address for the life of the
+ *   process; make that first call before any stream capture, and do not reset the device
+ *   (cudaDeviceReset) while using this call.
  *   All calls on a device share the one scratch array: calls whose kernels can overlap on
  *   the GPU (different streams, or different host threads) race and corrupt each other's
  *   codes.  Order them on one stream.  Each call rewrites everything it reads back. */

@@ -7,7 +7,9 @@ and the C ABI of ``include/qlinear.h`` (``lib/libqlinear_b200.so``).
 """
 from .npu import Backend, Linear, NpuError, QuantMatrix  # noqa: F401
 from .projection import MatrixLoader, Projection, concatenate  # noqa: F401
+from .layers import DenseLayerLinears, OutputHead  # noqa: F401
 from ._lib import LIB_PATH, QLinearUnavailable, ROUND_AWAY, ROUND_EVEN  # noqa: F401
 
 __all__ = ["Backend", "Linear", "NpuError", "QuantMatrix", "LIB_PATH", "QLinearUnavailable",
-           "ROUND_AWAY", "ROUND_EVEN", "MatrixLoader", "Projection", "concatenate"]
+           "ROUND_AWAY", "ROUND_EVEN", "MatrixLoader", "Projection", "concatenate",
+           "DenseLayerLinears", "OutputHead"]

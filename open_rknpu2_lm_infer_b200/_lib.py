@@ -88,6 +88,7 @@ SIGNATURES = {
                                     _I, _P]),
     "qlinear_act_quant_device": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _P]),
     "qlinear_run_device_noalloc": (_I, [_P, _P, _I, _P, _I, ctypes.c_longlong, _I, _P]),
+    "qlinear_swiglu_device": (_I, [_P, _P, _I, _I, _P, _I, ctypes.c_longlong, _P]),
     "qlinear_interleave_columns": (_I, [_P, _P, _P, _I, _I, _I, _I, _P]),
     "qlinear_backend_profile": (_I, [_P, _I]),
     "qlinear_backend_profile_collect": (_I, [_P, ctypes.POINTER(ctypes.c_double),

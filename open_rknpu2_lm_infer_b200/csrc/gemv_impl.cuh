@@ -519,6 +519,15 @@ template <int BITS, int MT, bool SWIGLU, int U, bool SCATTER, bool BAL>
 __global__ void __launch_bounds__(kThreads, 1)
     gemv_kernel(const GemvArgs p, const typename OutsParam<SCATTER>::type outs) {
     extern __shared__ __align__(16) uint8_t smem[];
+    // Let the next call on the stream launch now: its CTAs take the SMs this grid frees one
+    // by one and stream their own weights while this grid drains.  Safe for any dependent
+    // this library launches with programmatic serialization (the GEMV and the GEMM): before
+    // their griddepcontrol.wait they only read their own weights and weight scales, which
+    // nothing writes while calls run, and they read activations and store outputs only
+    // after it (this grid complete, its stores visible).  Every other kernel is launched
+    // without programmatic serialization and starts after this grid completes.  The
+    // exchange kernels keep the implicit trigger at exit.
+    if constexpr (!SCATTER) asm volatile("griddepcontrol.launch_dependents;");
     gemv_body<BITS, MT, SWIGLU, U, SCATTER, BAL>(p, outs, smem, [] {
         asm volatile("griddepcontrol.wait;" ::: "memory");
         return true;

@@ -12,7 +12,9 @@
 // of codes plus scales and row sums): every GPU that loads the library holds it until the
 // process exits.  Host code cannot pass the array's name to a kernel (on the host it is a
 // stand-in, not a device address), so the first call on each device, with that device
-// current, looks its address up with cudaGetSymbolAddress and keeps it.  All calls on a
+// current, looks its address up with cudaGetSymbolAddress and keeps it for the life of the
+// process (a cudaDeviceReset, which unloads the library's device code, is not supported
+// while this call is in use: the kept address would be stale).  All calls on a
 // device share the array; calls that overlap on the GPU race.  Nothing in it needs to start
 // at zero: act-quant rewrites the codes (and their K padding), scales and row sums of every
 // row the GEMV then reads.
@@ -50,6 +52,9 @@ extern "C" int qlinear_run_device_noalloc(const qlinear_weights *weights, const 
         (c_type != QLINEAR_F32 && c_type != QLINEAR_F16 && c_type != QLINEAR_I32) || ldc < v.N)
         return QLINEAR_ERR_PARAM;
     if (rows > kMaxRows || v.Kp > kMaxK) return QLINEAR_ERR_LIMIT;
+    // the GEMV's own shared-memory plan (very wide layers stage more scales per CTA than it
+    // holds): refused here, before anything is launched
+    if (!gemv_fits(rows, v.Kp, v.N, v.bits, false, num_sms)) return QLINEAR_ERR_LIMIT;
     if (device < 0 || device >= kMaxDevices) return QLINEAR_ERR_PARAM;
 
     int prev = -1;

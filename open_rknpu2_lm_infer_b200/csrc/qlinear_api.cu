@@ -865,6 +865,18 @@ int qlinear_dequant_device(qlinear_backend *b, const qlinear_weights *w, const i
     return QLINEAR_OK;
 }
 
+int qlinear_swiglu_device(qlinear_backend *b, const float *y_dev, int rows, int N, void *c_dev,
+                          int c_type, long long ldc, void *stream) {
+    if (!b || !y_dev || !c_dev || rows < 1 || N < 2 || N % 2 || ldc < N / 2 ||
+        (c_type != QLINEAR_F16 && c_type != QLINEAR_F32))
+        return QLINEAR_ERR_PARAM;
+    DeviceGuard guard(b->device);
+    QL_TRY(launch_swiglu(y_dev, rows, N, c_dev, c_type == QLINEAR_F16 ? kF16 : kF32, ldc,
+                         static_cast<cudaStream_t>(stream)));
+    b->launches++;
+    return QLINEAR_OK;
+}
+
 int qlinear_interleave_columns(qlinear_backend *b, const void *src, void *dst, int shards,
                                int rows, int shard_cols, int elem_bytes, void *stream) {
     if (!b || !src || !dst || shards < 1 || rows < 1 || shard_cols < 1 ||

@@ -247,6 +247,15 @@ class Backend:
             self.raw, gate_up._raw, down._raw, _ptr(a), _dtype_code(a), _ptr(out), _dtype_code(out),
             down.n() if ldc is None else ldc, rows, stream), "MLP device run")
 
+    def swiglu_device(self, y, out, rows: int, n: int, ldc: int | None = None,
+                      stream=None) -> None:
+        """out[m][j] = silu(y[m][j]) * y[m][n/2 + j] for an f32 [rows][n] gate/up output on the
+        device (the reference's Cpu::swiglu fallback, src/model/dense.rs:509-523, for a
+        gate/up projection of two matrices)."""
+        _check(self._lib.qlinear_swiglu_device(self.raw, _ptr(y), rows, n, _ptr(out),
+                                               _dtype_code(out), n // 2 if ldc is None else ldc,
+                                               stream), "swiglu device")
+
     def row_amax_device(self, a, rows: int, k: int, amax, stream=None) -> None:
         """amax[m] = max |a[m][:k]| (device buffers; NaN ignored like Rust's f32::max)."""
         _check(self._lib.qlinear_row_amax_device(self.raw, _ptr(a), _dtype_code(a), rows, k,

@@ -229,8 +229,13 @@ class ShardedMLP:
         ordered after the kernels through it."""
         import torch
         import torch.distributed as dist
+        current = torch.cuda.current_stream(a.device).cuda_stream
         if stream is None:
-            stream = torch.cuda.current_stream(a.device).cuda_stream
+            stream = current
+        if stream != current:
+            # the all-reduces below run on torch's current stream: another stream would let
+            # them start before the kernels that produce their inputs have finished
+            raise ValueError("ShardedMLP.run_device: `stream` must be torch's current stream")
         dev = a.device
         mid = self._buf("mid", (rows, self.hs), torch.float32, dev)
         amax = self._buf("amax", (rows,), torch.float32, dev)

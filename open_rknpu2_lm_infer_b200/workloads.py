@@ -105,3 +105,63 @@ def narrow_kat(n: int, k: int = 2560, rows: int = 7):
     x = (((j * 17 + j // k * 3) % 127).astype(np.float32) / np.float32(63.0)
          - np.float32(1.0)).reshape(rows, k)
     return codes, scales.astype(np.float32), x
+
+
+# The Qwen3-4B-shaped dense model of the 36-layer configuration.
+QWEN3_4B = {"hidden": 2560, "q_heads": 32, "kv_heads": 8, "head_dim": 128,
+            "intermediate": 9728, "vocab": 151936, "layers": 36}
+
+
+def cfg3_module_bits(layers: int = 36, seed: int = SEED) -> dict[str, int]:
+    """Module name -> bits for the 36-layer configuration: the per-layer draw of
+    ``layer_bits`` applied to the modules of each linear (q/k/v share the fused q/k/v
+    linear's draw, gate/up the gate/up linear's); the W8 lm_head."""
+    out = {"lm_head": 8}
+    for i, (qkv, o, gu, down) in enumerate(layer_bits(layers, seed)):
+        p = f"model.layers.{i}."
+        for m in ("q_proj", "k_proj", "v_proj"):
+            out[p + "self_attn." + m] = qkv
+        out[p + "self_attn.o_proj"] = o
+        out[p + "mlp.gate_proj"] = gu
+        out[p + "mlp.up_proj"] = gu
+        out[p + "mlp.down_proj"] = down
+    return out
+
+
+class SyntheticCheckpoint:
+    """Seeded stand-in for a quantized checkpoint, behind the loader interface the projection
+    code takes (``bits(name)``, ``load(name, n, k) -> QuantMatrix``, the roles of
+    src/model/checkpoint.rs:320-389).  Codes and scales of a module come from a sub-stream
+    derived from its name, so every module differs and every load is reproducible.  With
+    ``share_by_shape`` modules of one (bits, K, N) share codes (the benchmark's cheaper
+    draw of a 36-layer model; every module is still uploaded separately)."""
+
+    def __init__(self, bits: dict[str, int], seed: int = SEED, share_by_shape: bool = False):
+        self._bits = dict(bits)
+        self.seed = seed
+        self.share_by_shape = share_by_shape
+        self._cache = {}
+
+    def bits(self, name: str) -> int:
+        return self._bits[name]
+
+    def stream_of(self, name: str, k: int, n: int) -> int:
+        import zlib
+        key = f"{self._bits[name]}:{k}:{n}" if self.share_by_shape else name
+        return 100000 + zlib.crc32(key.encode()) % 1000000
+
+    def codes(self, name: str, n: int, k: int):
+        """(codes int8 [k][n], scales f32 [n]) of a module."""
+        s = self.stream_of(name, k, n)
+        hit = self._cache.get(s)
+        if hit is None:
+            bits = self._bits[name]
+            hit = (weight_codes(bits, k, n, self.seed, s), weight_scales(n, self.seed, s))
+            if self.share_by_shape:
+                self._cache[s] = hit
+        return hit
+
+    def load(self, name: str, n: int, k: int):
+        from .npu import QuantMatrix
+        c, s = self.codes(name, n, k)
+        return QuantMatrix(self._bits[name], k, n, c, s)

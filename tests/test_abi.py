@@ -61,3 +61,12 @@ def test_no_cpu_fallback_when_library_missing(tmp_path):
     from open_rknpu2_lm_infer_b200 import _lib
     with pytest.raises(_lib.QLinearUnavailable):
         _lib.load(str(tmp_path / "libqlinear_b200.so"))
+
+
+def test_noalloc_limits_match_the_header():
+    """The Python constants of the allocation-free call's limits are the header's."""
+    from open_rknpu2_lm_infer_b200 import _lib
+    text = open(HEADER).read()
+    defs = dict(re.findall(r"#define\s+(QLINEAR_NOALLOC_\w+)\s+(\d+)", text))
+    assert int(defs["QLINEAR_NOALLOC_MAX_ROWS"]) == _lib.NOALLOC_MAX_ROWS
+    assert int(defs["QLINEAR_NOALLOC_MAX_K"]) == _lib.NOALLOC_MAX_K

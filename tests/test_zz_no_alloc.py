@@ -48,6 +48,35 @@ def test_noalloc_matches_regular_call_twice():
     backend.close()
 
 
+def test_noalloc_allocates_nothing_and_honours_ldc():
+    """After a first call (which looks up the scratch's address), further calls leave the
+    device's free memory and the backend's workspaces as they were; an output of row stride
+    ldc > N receives exactly its N columns per row."""
+    lib = L.load()
+    backend = Backend(device=0)
+    bits, k, n, rows, ldc = 4, 2560, 640, 6, 700
+    lin = backend.load(QuantMatrix(bits, k, n, W.weight_codes(bits, k, n, stream=77),
+                                   W.weight_scales(n, stream=77)))
+    xs = [torch.from_numpy(W.activations(rows, k, stream=s)).cuda() for s in (78, 79)]
+    want = torch.zeros((rows, n), dtype=torch.float16, device="cuda")
+    got = torch.full((rows, ldc), -3.0, dtype=torch.float16, device="cuda")
+    assert noalloc(lib, lin, xs[0], got, rows, ldc=ldc) == L.QLINEAR_OK  # first call: set-up
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    ws0 = backend.stats()["workspace_payload_bytes"]
+    for i in range(6):
+        assert noalloc(lib, lin, xs[i % 2], got, rows, ldc=ldc) == L.QLINEAR_OK
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
+    assert backend.stats()["workspace_payload_bytes"] == ws0
+    lin.run_device(xs[1], want, rows)
+    torch.cuda.synchronize()
+    assert torch.equal(got[:, :n], want)
+    assert torch.all(got[:, n:] == -3.0)
+    lin.close()
+    backend.close()
+
+
 def test_noalloc_rejects_sizes_beyond_its_scratch():
     lib = L.load()
     backend = Backend(device=0)
