@@ -67,7 +67,7 @@ def parse():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg4")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="target CPU time of the oracle baseline sample")
-    ap.add_argument("--exchange", choices=["gather", "fused"], default="fused",
+    ap.add_argument("--exchange", choices=["gather", "fused", "multicast"], default="fused",
                     help="split-N output exchange at N>1: NCCL all-gather + column assembly, "
                          "or the kernels' epilogues storing into every rank's buffer")
     ap.add_argument("--no-decode", action="store_true")
@@ -82,6 +82,8 @@ def parse():
                     help="comma-separated case-name prefixes to run with --sweep (default all)")
     ap.add_argument("--swiglu-unfused", action="store_true",
                     help="prefill SwiGLU as GEMM -> f32 workspace -> SwiGLU pass (comparison)")
+    ap.add_argument("--w4-packed-only", action="store_true",
+                    help="W4 weights without their int8 copy (the prefill GEMM unpacks them)")
     ap.add_argument("--stream-k", action="store_true",
                     help="let the GEMM choose its stream-K schedule (QLINEAR_BACKEND_GEMM_STREAM_K)")
     ap.add_argument("--mlp", action="store_true",
@@ -250,12 +252,13 @@ def parity_record(y_gpu_rows, y_oracle, idx):
 def workload_config(args, world):
     """The `config` object of the JSON line; both arms print the same one."""
     bits, k, n, m, desc = WORKLOADS[args.workload]
-    fused = args.exchange == "fused"
     return {"workload": desc, "M": m, "K": k, "N": n, "bits": bits,
             "parallelism": f"split-N x{world}" + (
                 "" if world == 1 else
                 " + output exchange fused into the kernels (NVLink peer stores)"
-                if fused else " + NCCL all-gather"),
+                if args.exchange == "fused" else
+                " + output exchange fused into the kernels (NVSwitch multicast stores)"
+                if args.exchange == "multicast" else " + NCCL all-gather"),
             "l2": "flushed (256 MiB write) between timed steps, outside the timed region",
             "inputs": "fp16 N(0,1) with 1% x20 outlier channels, seed 42"}
 
@@ -319,18 +322,19 @@ def run_ours(args, rank, world, local_rank):
     ns = n // world
     n0 = rank * ns
 
-    backend = Backend(device=local_rank)
+    backend = Backend(device=local_rank, w4_packed_only=args.w4_packed_only)
     codes = W.weight_codes(bits, k, n)
     scales = W.weight_scales(n)
     qm = QuantMatrix(bits, k, n, codes, scales)
     sharded = None
-    fused = args.exchange == "fused"
+    fused = args.exchange in ("fused", "multicast")
     if world > 1:
         # split-N; the [M][N] output put together on every rank either by an NCCL all-gather
         # of the slabs + column assembly, or (fused) by the kernels' epilogues storing each
         # rank's columns into every rank's buffer over NVLink
         from open_rknpu2_lm_infer_b200.sharded import ShardedLinear
-        sharded = ShardedLinear(backend, qm, fused_exchange=fused, max_rows=m)
+        sharded = ShardedLinear(backend, qm, fused_exchange=fused, max_rows=m,
+                                multicast=args.exchange == "multicast")
         lin = sharded.linear
     else:
         lin = backend.load_shard(qm, n0, n0 + ns)
@@ -619,7 +623,7 @@ def e2e_measure(backend, lin, torch, dist, dev, args, world, m, k, n, ns, x_host
         pin_in = torch.from_numpy(xin).pin_memory()
         pin_out = torch.empty((m, n), dtype=torch.float32).pin_memory()
         xd = torch.empty((m, k), dtype=torch.float32, device=dev)
-        fused = args.exchange == "fused"
+        fused = args.exchange in ("fused", "multicast")
         if fused:
             sharded.add_exchange(m, torch.float32)  # the host API's type
         else:
@@ -653,6 +657,8 @@ def e2e_measure(backend, lin, torch, dist, dev, args, world, m, k, n, ns, x_host
             "api": "qlinear_run_f32 (host f32 in/out)" if world == 1 else
                    "H2D f32 -> qlinear_run_device_scatter (fused NVLink output exchange) -> "
                    "D2H f32" if args.exchange == "fused" else
+                   "H2D f32 -> qlinear_run_device_multicast (NVSwitch multicast output "
+                   "exchange) -> D2H f32" if args.exchange == "multicast" else
                    "H2D f32 -> qlinear_run_device -> NCCL all-gather -> "
                    "qlinear_interleave_columns -> D2H f32"}
 
@@ -676,7 +682,7 @@ def run_mlp(args, rank, world, local_rank):
                           W.weight_scales(2 * h, stream=90))
     down = QuantMatrix(8, h, hidden, W.weight_codes(8, h, hidden, stream=91),
                        W.weight_scales(hidden, stream=91))
-    backend = Backend(device=local_rank)
+    backend = Backend(device=local_rank, w4_packed_only=args.w4_packed_only)
     x = torch.from_numpy(W.activations(m, hidden, stream=92)).to(dev)
     y = torch.empty((m, hidden), dtype=torch.float16, device=dev)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
@@ -745,7 +751,8 @@ def run_sweep(args):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    backend = Backend(device=0, swiglu_unfused=args.swiglu_unfused, gemm_stream_k=args.stream_k)
+    backend = Backend(device=0, swiglu_unfused=args.swiglu_unfused, gemm_stream_k=args.stream_k,
+                      w4_packed_only=args.w4_packed_only)
     stream = torch.cuda.current_stream(dev).cuda_stream
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size
     hbm = measured_peaks().get("hbm_gbs", 6650.0)
@@ -785,9 +792,10 @@ def run_sweep(args):
         return max(2, min(16, -(-4 * l2 // max(1, bytes_per_copy))))
 
     def kernel_bytes(bits, k, n, m):
-        """Weight bytes the path's kernel reads: the packed W4 copy for the decode GEMV
-        (M <= 8), the int8 copy otherwise (W4 prefill reads its int8 expansion)."""
-        wb = k * n * (bits // 8 if bits == 8 else (1 if m > 8 else 0.5))
+        """Weight bytes the path's kernel reads: the packed W4 copy, except for a W4
+        prefill GEMM of a backend that keeps the int8 expansion (it reads that)."""
+        w4_int8 = m > 8 and backend.stats().get("w4_prefill") == "int8 copy"
+        wb = k * n * (bits // 8 if bits == 8 else (1 if w4_int8 else 0.5))
         return int(wb) + 4 * n
 
     def emit(case, m, secs, ops, bytes_, launches, extra=None):

@@ -210,6 +210,21 @@ QLINEAR_API int qlinear_run_device_scatter(qlinear_backend *backend, const qline
                                            int ndev, int c_type, long long ldc, long long col_offset,
                                            int rows, unsigned flags, void *stream);
 
+/* The split-N exchange through NVSwitch multicast (no reference counterpart): as
+ * qlinear_run_device_scatter without SwiGLU, with mc_dev the multicast address (NVLS) bound to
+ * every rank's exchange buffer (the same layout as c_devs[], whose first entry is this GPU's
+ * own).  The tensor-core GEMM (rows above the decode path's 8) stores each output element
+ * once through mc_dev and the switch writes it into every rank's buffer, so each GPU sends
+ * its columns over NVLink once instead of once per peer; the decode GEMV stores to c_devs[]
+ * as qlinear_run_device_scatter does.  fp16 output: col_offset and ldc must be even
+ * (multimem stores are 32 bits wide).  The kernels end with a system-scope fence, as for
+ * qlinear_run_device_scatter. */
+QLINEAR_API int qlinear_run_device_multicast(qlinear_backend *backend,
+                                             const qlinear_weights *weights, const void *a_dev,
+                                             int a_type, void *const *c_devs, int ndev,
+                                             void *mc_dev, int c_type, long long ldc,
+                                             long long col_offset, int rows, void *stream);
+
 /* Exchange buffers for qlinear_run_device_scatter: qlinear_peer_buffer_create allocates
  * `bytes` of device memory on the backend's GPU and writes its CUDA IPC handle
  * (QLINEAR_IPC_HANDLE_BYTES bytes) to ipc_handle; another process opens that handle with

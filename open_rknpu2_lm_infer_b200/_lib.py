@@ -76,6 +76,8 @@ SIGNATURES = {
     "qlinear_selftest_wait_timeout": (_I, [_P, ctypes.c_ulonglong]),
     "qlinear_run_device_scatter": (_I, [_P, _P, _P, _I, _P, _I, _I, ctypes.c_longlong,
                                         ctypes.c_longlong, _I, ctypes.c_uint, _P]),
+    "qlinear_run_device_multicast": (_I, [_P, _P, _P, _I, _P, _I, _P, _I, ctypes.c_longlong,
+                                          ctypes.c_longlong, _I, _P]),
     "qlinear_peer_buffer_create": (_I, [_P, ctypes.c_size_t, _P, _P]),
     "qlinear_peer_buffer_open": (_I, [_P, _P, _P]),
     "qlinear_peer_buffer_free": (_I, [_P, _P, _I]),

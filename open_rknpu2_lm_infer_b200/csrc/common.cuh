@@ -167,6 +167,23 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 __device__ __forceinline__ void tmem_ld_wait() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// 32 lanes x 32 bit, 32 consecutive columns per thread (the warp's own lane quadrant).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+        "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+        "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+        "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+// Wait until this thread's tcgen05.st writes have completed.
+__device__ __forceinline__ void tmem_st_wait() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
 
 
 // ------------------------------------------------------------------ clusters (CTA pairs)
@@ -188,6 +205,16 @@ __device__ __forceinline__ void cluster_sync() {
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                  : "memory");
+}
+// Arrive on a peer CTA's mbarrier to announce tensor-memory work (tcgen05.st or tcgen05.ld)
+// that the arriving thread has waited for (tcgen05.wait) and fenced
+// (tcgen05.fence::before_thread_sync): release at CTA scope, the default of the instruction.
+// The cluster-scope release above also orders the thread's generic memory accesses for the
+// peer, which this hand-off does not need; measured on B200 it held the packed-W4 GEMM (whose
+// converter warps hand every stage to the pair's MMA thread this way) at 0.66 POPS against
+// 1.1 POPS with this form (cfg4, M=512).
+__device__ __forceinline__ void mbar_arrive_remote_tc(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 __device__ __forceinline__ void mbar_arrive_expect_tx_remote(uint32_t cluster_addr, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(
@@ -228,6 +255,18 @@ __device__ __forceinline__ void mma_i8_ss_pair(uint32_t d_tmem, uint64_t adesc, 
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// The same with A read from tensor memory: each CTA's 128 rows of A sit in its own tensor
+// memory at a_tmem (lane = row, four 8-bit codes per 32-bit column, 8 columns per K = 32),
+// B from shared memory as above.  Issued by the leader CTA.
+__device__ __forceinline__ void mma_i8_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                               uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 // Arrive once on the same mbarrier offset in every CTA of `mask` when all prior
@@ -320,6 +359,13 @@ __device__ __forceinline__ int a8_code(float v, float inv, int round_mode) {
     const float r = round_mode ? rintf(s) : roundf(s);
     const int q = (r != r) ? 0 : __float2int_rz(r);
     return max(-127, min(127, q));
+}
+
+// 32-bit store through an NVSwitch multicast address (the NVLS mapping of every rank's
+// buffer): one store, written by the switch into every GPU's copy.  Multimem stores are at
+// least 32 bits wide.
+__device__ __forceinline__ void multimem_st_b32(const void *mc_addr, uint32_t v) {
+    asm volatile("multimem.st.global.b32 [%0], %1;" ::"l"(mc_addr), "r"(v) : "memory");
 }
 
 // Output element store helpers (f32 / f16 / raw i32).

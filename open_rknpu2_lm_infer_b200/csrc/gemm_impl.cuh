@@ -59,12 +59,25 @@ constexpr int KB = GEMM_KB;                 // k-block depth (int8 codes per row
 static_assert(KB == 128, "one 128-byte swizzle atom per row per stage");
 constexpr int CH_CTA = CH_TILE;             // 128 channels per CTA
 constexpr int CHT = 2 * CH_CTA;             // 256 channels per pair tile
-constexpr int A_SLOT = CH_CTA * KB;         // 16 KB unpacked weights per CTA
-constexpr int W4_PREFETCH = 4;              // converter register ring depth (k-blocks)
+constexpr int A_SLOT = CH_CTA * KB;         // 16 KB 8-bit weights per CTA per stage
+constexpr int P_SLOT = CH_CTA * KB / 2;     // 8 KB packed W4 weights per CTA per stage
+// W4: the unpacked weights live in tensor memory, a ring of A_SLOTS 32-column slots (128 codes
+// of each of the CTA's 128 channels per k-block) after the two accumulator buffers; so the
+// token tile is at most 128 (2 x 128 accumulator columns).  The shared-memory ring of
+// activation and packed-weight tiles is deeper (up to MAX_STAGES_W4), so the copies run
+// further ahead of the unpacking.
+constexpr uint32_t A_TMEM_COL = 256;
+constexpr int W4_MAX_TOK = 128;
+#ifndef QL_W4_CONV_BATCH
+#define QL_W4_CONV_BATCH 1
+#endif
+constexpr int W4_CONV_BATCH = QL_W4_CONV_BATCH;  // stages a converter warp unpacks per wait
 constexpr int EPI_WARPS = 8;
 constexpr int MAX_DYN_SMEM = 232448;        // 227 KB opt-in per block on sm_100
 constexpr int SMEM_RESERVE = 1024 + 1024;   // alignment slack + barriers
 constexpr int MAX_STAGES = 8;
+constexpr int MAX_STAGES_W4 = 12;           // W4: a 16 KB stage (activations + packed weights)
+constexpr int A_SLOTS = 8;                  // W4: unpacked-weight slots in tensor memory
 // Stream-K workspace: the contribution counters first, at a fixed place for every plan (they
 // must be zero before each launch, and the partial-sum buffers after them are overwritten
 // with plan-dependent layouts), room for SK_MAX_PAIRS pairs x 2 * EPI_WARPS sub-blocks.
@@ -251,22 +264,30 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap amap,
                 const GemmArgs p, const OutputSet outs,
                 const __grid_constant__ CUtensorMap amap_sub) {
-    constexpr bool SCATTER = NDST > 1;
+    // NDST == 0: one destination, the NVSwitch multicast address of every rank's buffer
+    // (multimem stores: the switch writes each element into every GPU's copy)
+    constexpr bool MCAST = NDST == 0;
+    constexpr bool SCATTER = NDST > 1 || MCAST;
+    constexpr int NPTR = MCAST ? 1 : NDST;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                 ~uintptr_t(1023));
     const int S = p.stages;
     const int tok = p.tok;
     const int b_half = (tok / 2) * KB;                    // this CTA's activation rows
-    constexpr int w_slot = A_SLOT;   // 8-bit weights per stage (TMA for W8, converter for W4)
+    // weights per stage: W8 the [128][128] tile (128-byte swizzle), W4 the packed [128][64]
+    // tile (64-byte swizzle) that the converter unpacks into tensor memory
+    constexpr int w_slot = BITS == 8 ? A_SLOT : P_SLOT;
     uint8_t *sB = smem;              // [S][tok/2][128]
-    uint8_t *sW = sB + S * b_half;   // [S][128][128]
+    uint8_t *sW = sB + S * b_half;   // [S][w_slot]
     uint64_t *bars = reinterpret_cast<uint64_t *>(sW + S * w_slot);
-    uint64_t *full = bars;              // [S] leader: both CTAs' TMA bytes landed
+    uint64_t *full = bars;              // [S] leader: both CTAs' activation (W8: + weight) bytes
     uint64_t *empty = full + S;         // [S] the MMA is done with the stage
-    uint64_t *afull = empty + S;        // [S] leader: both converters unpacked the stage
-    uint64_t *cdone = afull + S;        // [S] W4: this CTA's 128 converter threads wrote it
-    uint64_t *accf = cdone + S;         // [2] accumulators ready for the epilogue
+    uint64_t *wfull = empty + S;        // [S] W4: this CTA's packed weight tile landed
+    uint64_t *afull = wfull + S;        // [A_SLOTS] W4, leader: both converters filled the slot
+    uint64_t *cdone = afull + A_SLOTS;  // [A_SLOTS] W4: this CTA's 128 converter threads did
+    uint64_t *aempty = cdone + A_SLOTS; // [A_SLOTS] W4: the MMA is done with the slot
+    uint64_t *accf = aempty + A_SLOTS;  // [2] accumulators ready for the epilogue
     uint64_t *acce = accf + 2;          // [2] leader: both epilogues drained them
     uint64_t *drain = acce + 2;         // [1] leader: MMA drain on abort
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
@@ -281,8 +302,12 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
         for (int s = 0; s < S; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
-            mbar_init(&afull[s], 2);
-            mbar_init(&cdone[s], 128);
+            mbar_init(&wfull[s], 1);
+        }
+        for (int a = 0; a < A_SLOTS; a++) {
+            mbar_init(&afull[a], 2);
+            mbar_init(&cdone[a], 128);
+            mbar_init(&aempty[a], 1);
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&accf[b], 1);
@@ -316,7 +341,21 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
         if (lane == 0) {
             // tx: the bytes the leader's `full` barrier receives for the stage from both CTAs
             auto load_weights = [&](int s, int kb, int tc, uint32_t tx) {
-                if constexpr (GLU) {
+                if constexpr (BITS == 4) {
+                    // this CTA's packed tile, counted on its own barrier (the converter's)
+                    if constexpr (GLU) {
+#pragma unroll
+                        for (int b = 0; b < 8; b++)
+                            tma_load_2d(sW + s * w_slot + b * 16 * (KB / 2), &wmap, &wfull[s],
+                                        kb * (KB / 2),
+                                        (b & 1) * (p.N / 2) + tc * CH_CTA + (int)rank * 64 +
+                                            (b >> 1) * 16);
+                    } else {
+                        tma_load_2d(sW + s * w_slot, &wmap, &wfull[s], kb * (KB / 2),
+                                    tc * CHT + (int)rank * CH_CTA);
+                    }
+                    mbar_arrive_expect_tx(&wfull[s], (uint32_t)P_SLOT);
+                } else if constexpr (GLU) {
                     // quadrant q: gate rows c0 .. c0 + 15, then up rows N/2 + c0 ..
 #pragma unroll
                     for (int b = 0; b < 8; b++)
@@ -371,6 +410,7 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                 const uint32_t first = issued > (uint32_t)S ? issued - S : 0;
                 for (uint32_t j = first; j < issued; j++) {
                     if (rank == 0) mbar_wait(&full[j % S], (j / S) & 1, nullptr, &never);
+                    if (BITS == 4) mbar_wait(&wfull[j % S], (j / S) & 1, nullptr, &never);
                 }
             }
         }
@@ -378,6 +418,7 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
         // ------------------------------------------------------------ MMA issuer (leader)
         if (lane == 0 && rank == 0) {
             uint32_t s = 0, ph = 0, local = 0;
+            uint32_t as = 0, aph = 0;  // W4: tensor-memory slot of the unpacked weights
             bool ok = true;
             Sched sm(p, (int)cid, (int)ncl);
             int t, kb0, kb1;
@@ -391,15 +432,27 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                 const uint32_t idesc = idesc_i8(2 * CH_CTA, ntok, BITS == 8, true);
                 for (int kb = kb0; kb < kb1; kb++) {
                     if (!(ok = mbar_wait(&full[s], ph, err, abort_flag))) break;
-                    if (BITS == 4 && !(ok = mbar_wait(&afull[s], ph, err, abort_flag))) break;
+                    if (BITS == 4 && !(ok = mbar_wait(&afull[as], aph, err, abort_flag))) break;
                     tc_fence_after();
-                    const uint64_t adesc = smem_desc_sw128_k(sW + s * w_slot);
                     const uint64_t bdesc = smem_desc_sw128_k(sB + s * b_half);
+                    if constexpr (BITS == 4) {
+                        // A: the stage's unpacked weights in tensor memory, 8 columns per MMA
+                        const uint32_t at = tmem_base + A_TMEM_COL + 32u * as;
 #pragma unroll
-                    for (int k = 0; k < KB / 32; k++)
-                        mma_i8_ss_pair(d, adesc + 2 * k, bdesc + 2 * k, idesc, kb != kb0 || k != 0);
+                        for (int k = 0; k < KB / 32; k++)
+                            mma_i8_ts_pair(d, at + 8 * k, bdesc + 2 * k, idesc, kb != kb0 || k != 0);
+                    } else {
+                        const uint64_t adesc = smem_desc_sw128_k(sW + s * w_slot);
+#pragma unroll
+                        for (int k = 0; k < KB / 32; k++)
+                            mma_i8_ss_pair(d, adesc + 2 * k, bdesc + 2 * k, idesc, kb != kb0 || k != 0);
+                    }
                     mma_commit_pair(&empty[s], 0x3);
                     if (++s == (uint32_t)S) { s = 0; ph ^= 1; }
+                    if constexpr (BITS == 4) {
+                        mma_commit_pair(&aempty[as], 0x3);
+                        if (++as == (uint32_t)A_SLOTS) { as = 0; aph ^= 1; }
+                    }
                 }
                 if (ok) mma_commit_pair(&accf[ab], 0x3);
             }
@@ -436,14 +489,61 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
         // The exchange's destinations, held in registers.  (Measured on B200: a predicated
         // store per slot of the parameter array made a 16-token chunk's stores ~5x slower
         // than these unconditional ones.)
-        OutT *od[NDST];
+        OutT *od[NPTR];
         if constexpr (SCATTER) {
 #pragma unroll
-            for (int d = 0; d < NDST; d++) od[d] = static_cast<OutT *>(outs.dst[d]) + outs.col0;
+            for (int d = 0; d < NPTR; d++) od[d] = static_cast<OutT *>(outs.dst[d]) + outs.col0;
         }
+        // Multicast stores of chunk cc: multimem stores are at least 32 bits wide, so for fp16
+        // the lanes of a pair (channels 2i, 2i + 1) swap one value per token pair and each
+        // stores one channel pair: the even lane token 2t, the odd lane token 2t + 1.  (The
+        // output's column offset and row stride are even, so the pair is 4-byte aligned.)
+        auto emit16_mc = [&](const uint32_t (&r)[16], int cc, int tok_base, int ch, bool chv,
+                             float sw) {
+            uint32_t v[16];
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const int src = (cc & 1) * 16 + j;
+                const float sa = __shfl_sync(0xffffffffu, sa_r[cc >> 1], src);
+                const int rs = __shfl_sync(0xffffffffu, rs_r[cc >> 1], src);
+                int acc = (int)r[j];
+                if (BITS == 4) acc -= 8 * rs;
+                if constexpr (std::is_same<OutT, int32_t>::value)
+                    v[j] = (uint32_t)acc;
+                else if constexpr (std::is_same<OutT, float>::value)
+                    v[j] = __float_as_uint(__fmul_rn(__fmul_rn(__int2float_rn(acc), sa), sw));
+                else
+                    v[j] = (uint32_t)__half_as_ushort(
+                        __float2half_rn(__fmul_rn(__fmul_rn(__int2float_rn(acc), sa), sw)));
+            }
+            const int m0 = tok_base + cc * 16;
+            if constexpr (std::is_same<OutT, __half>::value) {
+                const bool odd = (lane & 1) != 0;
+#pragma unroll
+                for (int t = 0; t < 8; t++) {
+                    const uint32_t other =
+                        __shfl_xor_sync(0xffffffffu, odd ? v[2 * t] : v[2 * t + 1], 1);
+                    const int m = m0 + 2 * t + (odd ? 1 : 0);
+                    if (chv && m < p.M) {
+                        const uint32_t pair = odd ? (other | (v[2 * t + 1] << 16))
+                                                  : (v[2 * t] | (other << 16));
+                        multimem_st_b32(od[0] + (long long)m * p.ldc + (ch & ~1), pair);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; j++)
+                    if (chv && m0 + j < p.M)
+                        multimem_st_b32(od[0] + (long long)(m0 + j) * p.ldc + ch, v[j]);
+            }
+        };
         // dequantise and store chunk cc (columns 16 cc .. 16 cc + 15 of the warp's range)
         auto emit16 = [&](const uint32_t (&r)[16], int cc, int tok_base, int ch, bool chv,
                           float sw) {
+            if constexpr (MCAST) {
+                emit16_mc(r, cc, tok_base, ch, chv, sw);
+                return;
+            }
 #pragma unroll
             for (int j = 0; j < 16; j++) {
                 const int src = (cc & 1) * 16 + j;
@@ -469,7 +569,7 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                                 __fmul_rn(__fmul_rn(__int2float_rn(acc), sa), sw));
                         const long long idx = (long long)m * p.ldc + ch;
 #pragma unroll
-                        for (int d = 0; d < NDST; d++) od[d][idx] = v;
+                        for (int d = 0; d < NPTR; d++) od[d][idx] = v;
                     }
                 }
             }
@@ -539,7 +639,7 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive_remote(acce0 + 8u * ab);
+                if (lane == 0) mbar_arrive_remote_tc(acce0 + 8u * ab);
                 continue;
             }
             // A segment of a split tile.  Its partial sums go to its own workspace buffer
@@ -569,7 +669,7 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_remote(acce0 + 8u * ab);  // tensor memory is free
+            if (lane == 0) mbar_arrive_remote_tc(acce0 + 8u * ab);  // tensor memory is free
             __threadfence();
             __syncwarp();
             int last = 0;
@@ -630,76 +730,74 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
         if constexpr (SCATTER) __threadfence_system();
     } else {
         // ------------------------------------------------------------ W4 converter
+        // Thread (warp w, lane l) owns tensor-memory lane 32 (w % 4) + l, i.e. row 32 (w % 4) + l
+        // of the CTA's weight slot (a warp may only access its own lane quadrant).  Per stage
+        // it reads its row's 64 packed bytes from shared memory (64-byte swizzle: 16-byte
+        // chunk c of row r sits at chunk c ^ ((r >> 1) & 3), so the warp's reads are
+        // conflict-free), unpacks them and writes the 128 codes to the stage's 32 columns
+        // of tensor memory.  Nibbles stay offset-binary (u = code + 8; A is declared
+        // unsigned), so the unpack is two masks per word and the epilogue subtracts
+        // 8 * sum_k q[m][k].  Word i of a row's 16 covers k = 8i .. 8i + 7: its low nibbles
+        // k 8i .. 8i + 3 (column 2i), its high nibbles 8i + 4 .. 8i + 7 (column 2i + 1).
         if constexpr (BITS == 4) {
             const int ct = threadIdx.x - (2 + EPI_WARPS) * 32;  // 0..127
-            const int cp = ct & 3;      // 16-byte quarter of a row's 64 packed bytes (32 codes)
-            const int r0 = ct >> 2;     // rows r0 + 32 j, j = 0..3
-            const long long row_bytes = (long long)p.nkb * (KB / 2);
-            // Packed codes of iteration (tile t, k-block kb) for this thread's 4 rows.
-            auto fetch = [&](uint4 (&b)[4], int t, int kb) {
-                int tc, tok0, ntok;
-                tile_geom(p, t, tc, tok0, ntok);
-                const int n0 = tc * CHT + (int)rank * CH_CTA;
+            const int q = warp & 3;
+            const int row = q * 32 + lane;
+            const int swz = (row >> 1) & 3;
+            const uint32_t tcol = tmem_base + ((uint32_t)(q * 32) << 16) + A_TMEM_COL;
+            uint32_t s = 0, ph = 0;    // shared-memory stage of the packed tile
+            uint32_t as = 0, aph = 0;  // tensor-memory slot it is unpacked into
+            Units cu(p, (int)cid, (int)ncl);
+            bool okw = true;
+            while (cu.live && okw) {
+                // W4_CONV_BATCH stages per round: their tensor-memory writes complete under
+                // one tcgen05.wait::st before the stages are announced
+                uint32_t bs[W4_CONV_BATCH], bp[W4_CONV_BATCH];
+                int nb = 0;
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const int n = n0 + r0 + 32 * j;
-                    b[j] = n < p.Np ? ldg_stream(p.wq + (long long)n * row_bytes + kb * (KB / 2) +
-                                                 cp * 16)
-                                    : make_uint4(0, 0, 0, 0);
+                for (int b = 0; b < W4_CONV_BATCH; b++) {
+                    if (!cu.live) break;
+                    // the MMA released the tensor-memory slot (iteration it - A_SLOTS) and this
+                    // iteration's packed tile landed; the warp stays converged
+                    okw = mbar_wait(&aempty[as], aph ^ 1, err, abort_flag) &&
+                          mbar_wait(&wfull[s], ph, err, abort_flag);
+                    if (!__all_sync(0xffffffffu, okw)) { okw = false; break; }
+                    const uint8_t *P = sW + s * w_slot + row * (KB / 2);
+                    uint32_t u[32];
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        const uint4 v = *reinterpret_cast<const uint4 *>(P + 16 * (c ^ swz));
+                        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            u[8 * c + 2 * i] = w4[i] & 0x0F0F0F0Fu;
+                            u[8 * c + 2 * i + 1] = (w4[i] >> 4) & 0x0F0F0F0Fu;
+                        }
+                    }
+                    tmem_st32(tcol + 32u * as, u);
+                    bs[nb] = as;
+                    bp[nb] = aph;
+                    nb++;
+                    if (++s == (uint32_t)S) { s = 0; ph ^= 1; }
+                    if (++as == (uint32_t)A_SLOTS) { as = 0; aph ^= 1; }
+                    cu.advance();
                 }
-            };
-            uint4 buf[W4_PREFETCH][4];
-            Units fu(p, (int)cid, (int)ncl);  // prefetch stream position
+                if (!okw) break;
+                tmem_st_wait();
+                // the writes before the arrivals, ordered for the MMAs issued after the wait
+                tc_fence_before();
 #pragma unroll
-            for (int u = 0; u < W4_PREFETCH; u++) {
-                if (fu.live) {
-                    fetch(buf[u], fu.t, fu.kb);
-                    fu.advance();
-                }
-            }
-            uint32_t s = 0, ph = 0;
-            Units cu(p, (int)cid, (int)ncl);  // the iteration being unpacked
-            bool live = cu.live;
-            while (live) {
+                for (int b = 0; b < W4_CONV_BATCH; b++)
+                    if (b < nb) mbar_arrive(&cdone[bs[b]]);
+                if (ct == 0) {
 #pragma unroll
-                for (int u = 0; u < W4_PREFETCH; u++) {
-                    if (live) {
-                        // the MMA released the stage (its A buffer) of iteration it - S
-                        if (!mbar_wait(&empty[s], ph ^ 1, err, abort_flag)) { live = false; break; }
-                        uint8_t *A = sW + s * w_slot;
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            const int row = r0 + 32 * j;
-                            const uint4 v = buf[u][j];
-                            // word p of the 16 packed bytes covers 8 codes: low nibbles
-                            // k 8p..8p+3, high nibbles 8p+4..8p+7 (k relative to 32*cp).
-                            const uint4 c0 = make_uint4(v.x & 0x0F0F0F0Fu, (v.x >> 4) & 0x0F0F0F0Fu,
-                                                        v.y & 0x0F0F0F0Fu, (v.y >> 4) & 0x0F0F0F0Fu);
-                            const uint4 c1 = make_uint4(v.z & 0x0F0F0F0Fu, (v.z >> 4) & 0x0F0F0F0Fu,
-                                                        v.w & 0x0F0F0F0Fu, (v.w >> 4) & 0x0F0F0F0Fu);
-                            const int sw = row & 7;  // 128-byte swizzle of this row
-                            *reinterpret_cast<uint4 *>(A + row * 128 + (((2 * cp) ^ sw) << 4)) = c0;
-                            *reinterpret_cast<uint4 *>(A + row * 128 + (((2 * cp + 1) ^ sw) << 4)) = c1;
-                        }
-                        // refill this register slot with the iteration W4_PREFETCH ahead
-                        if (fu.live) {
-                            fetch(buf[u], fu.t, fu.kb);
-                            fu.advance();
-                        }
-                        // every writer makes its stores visible to the async proxy and
-                        // arrives locally; one thread collects the 128 arrivals (bounded) and
-                        // announces the stage to the leader with one cluster-scope arrive
-                        fence_proxy_async_smem();
-                        mbar_arrive(&cdone[s]);
-                        if (ct == 0) {
-                            if (!mbar_wait(&cdone[s], ph, err, abort_flag)) live = false;
-                            else mbar_arrive_remote(afull0 + 8u * s);
-                        }
-                        if (++s == (uint32_t)S) { s = 0; ph ^= 1; }
-                        cu.advance();
-                        if (!cu.live) live = false;
+                    for (int b = 0; b < W4_CONV_BATCH; b++) {
+                        if (b >= nb || !okw) break;
+                        if (!mbar_wait(&cdone[bs[b]], bp[b], err, abort_flag)) okw = false;
+                        else mbar_arrive_remote_tc(afull0 + 8u * bs[b]);
                     }
                 }
+                okw = __all_sync(0xffffffffu, okw);
             }
         }
     }
@@ -768,7 +866,8 @@ inline GemmArgs make_args(const WeightView &w, const ActView &a, const GemmPlan 
     args.num_tiles = plan.tiles;
     uint32_t cols = 32;
     while (cols < (uint32_t)(2 * plan.tok)) cols <<= 1;
-    args.tmem_cols = cols;
+    // W4: the accumulators and the ring of unpacked weights (A_TMEM_COL + 8 x 32 columns)
+    args.tmem_cols = w.bits == 4 ? 512u : cols;
     args.err = err;
     args.sk_tiles = plan.sk_tiles;
     if (plan.sk == 2) {  // tail split: sub-tiles per split tile, no workspace

@@ -36,7 +36,13 @@ int gemm_pair_capacity(int bits) { return bits == 8 ? pair_capacity_t<8>() : pai
 
 GemmPlan plan_gemm(const WeightView &w, int rows, int max_pairs, bool allow_sk) {
     GemmPlan plan{};
-    const int tiles_m = std::max(1, (rows + 255) / 256);
+    // W4 keeps its unpacked weights in tensor memory beside the accumulators: token tiles
+    // of at most 128
+#ifndef QL_W8_MAX_TOK
+#define QL_W8_MAX_TOK 256
+#endif
+    const int tok_max = w.bits == 4 ? W4_MAX_TOK : QL_W8_MAX_TOK;
+    const int tiles_m = std::max(1, (rows + tok_max - 1) / tok_max);
     int tok = (rows + tiles_m - 1) / tiles_m;
     tok = std::max(32, (tok + 31) / 32 * 32);  // 2-CTA MMA: N multiple of 32
     // A narrow weight shard (split-N over many GPUs) leaves pairs idle: halve the token tile
@@ -50,9 +56,10 @@ GemmPlan plan_gemm(const WeightView &w, int rows, int max_pairs, bool allow_sk) 
             tok /= 2;
     }
     plan.tok = tok;
-    const int stage_bytes = (tok / 2) * KB + A_SLOT;
+    const int stage_bytes = (tok / 2) * KB + (w.bits == 8 ? A_SLOT : P_SLOT);
     const int fixed = SMEM_RESERVE;
-    const int stages = std::min(MAX_STAGES, (MAX_DYN_SMEM - fixed) / stage_bytes);
+    const int stages = std::min(w.bits == 4 ? MAX_STAGES_W4 : MAX_STAGES,
+                                (MAX_DYN_SMEM - fixed) / stage_bytes);
     plan.stages = stages;
     // One CTA per SM: each CTA of the pair allocates up to 512 TMEM columns.
     plan.smem_bytes = std::max(stages * stage_bytes + fixed, 120 * 1024);

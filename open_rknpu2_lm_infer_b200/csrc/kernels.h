@@ -141,6 +141,14 @@ cudaError_t launch_gemm_scatter(const WeightView &w, const CUtensorMap &wmap, co
                                 const OutputSet &out, int out_type, long long ldc, unsigned *err,
                                 void *sk_ws, bool pdl, cudaStream_t stream);
 
+// The split-N exchange's GEMM through an NVSwitch multicast address (out.dst[0]; fp16 needs
+// an even out.col0 and ldc).
+cudaError_t launch_gemm_multicast(const WeightView &w, const CUtensorMap &wmap, const ActView &a,
+                                  const CUtensorMap &amap, const CUtensorMap &amap_sub,
+                                  const GemmPlan &plan, int rows, const OutputSet &out,
+                                  int out_type, long long ldc, unsigned *err, void *sk_ws,
+                                  bool pdl, cudaStream_t stream);
+
 // Signal arrays of the split-N exchange's ranks (peer_sync.cu): sig[r] = rank r's, mapped here.
 struct PeerSignals {
     void *sig[kMaxOutputs];

@@ -180,12 +180,16 @@ bool tma_available() {
 bool encode_weight_map(const WeightView &w, CUtensorMap *map) {
     if (w.bits == 8)
         return encode_2d(map, w.w, w.Kp, w.Np, w.Kp, GEMM_KB, CH_TILE, CU_TENSOR_MAP_SWIZZLE_128B);
+    // packed W4 rows of 64 bytes per k-block; the 64-byte swizzle lets the converter's
+    // 128 threads (one row each) read the tile without bank conflicts
     return encode_2d(map, w.w, w.Kp / 2, w.Np, w.Kp / 2, GEMM_KB / 2, CH_TILE,
-                     CU_TENSOR_MAP_SWIZZLE_NONE);
+                     CU_TENSOR_MAP_SWIZZLE_64B);
 }
 bool encode_glu_map(const WeightView &w, CUtensorMap *map) {
-    if (w.bits != 8) return false;
-    return encode_2d(map, w.w, w.Kp, w.Np, w.Kp, GEMM_KB, 16, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (w.bits == 8)
+        return encode_2d(map, w.w, w.Kp, w.Np, w.Kp, GEMM_KB, 16, CU_TENSOR_MAP_SWIZZLE_128B);
+    return encode_2d(map, w.w, w.Kp / 2, w.Np, w.Kp / 2, GEMM_KB / 2, 16,
+                     CU_TENSOR_MAP_SWIZZLE_64B);
 }
 bool encode_act_map(const int8_t *codes, int rows_cap, int Kp, int tok, CUtensorMap *map) {
     return encode_2d(map, codes, Kp, rows_cap, Kp, GEMM_KB, tok / 2, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -292,9 +296,12 @@ int next_prof_events(qlinear_backend *b, const std::array<cudaEvent_t, 3> **out)
 // c_dev = outs.dst[0].
 // amax_in (optional, device [rows]): quantise with these row maxima (a K-split row's max over
 // every rank's slice) instead of each row's own.
+// mc (optional): the NVSwitch multicast address of the exchange buffers; the tensor-core GEMM
+// then stores through it once instead of to each of outs' destinations (the decode GEMV
+// still stores to outs).
 int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_dev, int a_type,
                     const OutputSet &outs, int c_type, long long ldc, int rows, unsigned flags,
-                    cudaStream_t stream, const float *amax_in = nullptr) {
+                    cudaStream_t stream, const float *amax_in = nullptr, void *mc = nullptr) {
     const WeightView &v = w->view;
     const bool swiglu = (flags & QLINEAR_RUN_SWIGLU) != 0;
     const int width = swiglu ? v.N / 2 : v.N;
@@ -378,7 +385,15 @@ int run_device_impl(qlinear_backend *b, const qlinear_weights *w, const void *a_
         st = get_amap(b, v.Kp, plan.tok / plan.split, &amap_sub);
         if (st) return st;
     }
-    if (!swiglu) {
+    if (!swiglu && mc) {
+        OutputSet mo{};
+        mo.dst[0] = mc;
+        mo.count = 1;
+        mo.col0 = outs.col0;
+        QL_TRY(launch_gemm_multicast(gv, gmap, av, *amap, *amap_sub, plan, rows, mo, c_type, ldc,
+                                     b->d_err, b->d_sk, true, stream));
+        b->launches++;
+    } else if (!swiglu) {
         QL_TRY(launch_gemm(gv, gmap, av, *amap, *amap_sub, plan, rows, outs, c_type, ldc,
                            b->d_err, b->d_sk, true, stream));
         b->launches++;
@@ -472,8 +487,10 @@ qlinear_weights *weights_create_common(qlinear_backend *b, const qlinear_weight_
         if (!encode_weight_map(w->view8, &w->wmap8)) return cleanup(QLINEAR_ERR_CUDA);
         w->bytes += bytes8;
     }
-    if (N % 2 == 0 && (v.bits == 8 || w->d_w8)) {
-        if (!encode_glu_map(v.bits == 8 ? v : w->view8, &w->wmap_glu))
+    if (N % 2 == 0) {
+        // the prefill weights' map in 16-row boxes: the 8-bit copy when there is one, else
+        // the packed W4 rows
+        if (!encode_glu_map(w->d_w8 ? w->view8 : v, &w->wmap_glu))
             return cleanup(QLINEAR_ERR_CUDA);
         w->has_glu = true;
     }
@@ -671,6 +688,23 @@ int qlinear_run_mlp_device(qlinear_backend *b, const qlinear_weights *gate_up,
     if (st) return st;
     return run_device_impl(b, down, b->d_mid, QLINEAR_F32, single_output(c_dev), c_type, ldc, rows,
                            0, s);
+}
+
+int qlinear_run_device_multicast(qlinear_backend *b, const qlinear_weights *w, const void *a_dev,
+                                 int a_type, void *const *c_devs, int ndev, void *mc_dev,
+                                 int c_type, long long ldc, long long col_offset, int rows,
+                                 void *stream) {
+    if (!b || !w || w->backend != b || !c_devs || !mc_dev || ndev < 1 || ndev > kMaxOutputs ||
+        col_offset < 0 || ldc < col_offset + w->view.N)
+        return QLINEAR_ERR_PARAM;
+    if (c_type == QLINEAR_F16 && ((col_offset | ldc) & 1)) return QLINEAR_ERR_PARAM;
+    OutputSet o{};
+    for (int d = 0; d < ndev; d++) o.dst[d] = c_devs[d];
+    o.count = ndev;
+    o.col0 = col_offset;
+    DeviceGuard guard(b->device);
+    return run_device_impl(b, w, a_dev, a_type, o, c_type, ldc, rows, 0,
+                           static_cast<cudaStream_t>(stream), nullptr, mc_dev);
 }
 
 int qlinear_run_device_scatter(qlinear_backend *b, const qlinear_weights *w, const void *a_dev,
@@ -970,13 +1004,14 @@ int qlinear_backend_stats(const qlinear_backend *b, char *buf, size_t len) {
         "\"strategy_fallback_calls\": 0, \"weight_reload_calls\": 0, \"round_mode\": \"%s\", "
         "\"prepared_rows\": %d, \"kernel_launches\": %llu, \"gemv_calls\": %llu, "
         "\"gemm_calls\": %llu, \"gemm_stream_k_calls\": %llu, \"gemm_swiglu_fused_calls\": %llu, "
-        "\"mlp_calls\": %llu, "
+        "\"mlp_calls\": %llu, \"w4_prefill\": \"%s\", "
         "\"gemm_pairs_resident\": [%d, %d]}",
         b->device, b->num_sms, b->loaded_w4, b->loaded_w8, (unsigned long long)b->weight_bytes,
         (unsigned long long)ws, b->ws_bytes ? 1 : 0,
         (unsigned long long)(b->h_in_bytes + b->h_out_bytes),
         b->round_mode == QLINEAR_ROUND_AWAY ? "away" : "even", b->prepared_rows, b->launches,
         b->gemv_calls, b->gemm_calls, b->gemm_stream_k_calls, b->gemm_glu_calls, b->mlp_calls,
+        (b->flags & QLINEAR_BACKEND_W4_PACKED_ONLY) ? "packed" : "int8 copy",
         b->gemm_pairs[0], b->gemm_pairs[1]);
     if (n < 0) return QLINEAR_ERR_PARAM;
     if (buf && len) {

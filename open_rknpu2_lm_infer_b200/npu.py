@@ -393,6 +393,21 @@ class Linear:
             self._backend.raw, self._raw, _ptr(acc), self._n, _ptr(row_amax), _ptr(out),
             _dtype_code(out), self._n, rows, stream), "dequant")
 
+    def run_device_multicast(self, a, outs, mc: int, out_type: int, ldc: int, col_offset: int,
+                             rows: int, stream=None) -> None:
+        """qlinear_run_device_multicast: as run_device_scatter, but the tensor-core GEMM stores
+        each output element once through `mc`, the NVSwitch multicast address bound to every
+        rank's exchange buffer (`outs`: their unicast addresses, this GPU's first, used by the
+        decode GEMV)."""
+        s = str(getattr(a, "dtype", ""))
+        a_type = L.F16 if "float16" in s else L.F32 if "float32" in s else None
+        if a_type is None:
+            raise TypeError(s)
+        arr = (ctypes.c_void_p * len(outs))(*[int(p) for p in outs])
+        _check(self._lib.qlinear_run_device_multicast(
+            self._backend.raw, self._raw, _ptr(a), a_type, arr, len(outs), int(mc), out_type,
+            ldc, col_offset, rows, stream), f"W{self.bits} device multicast run")
+
     def run_device_scatter(self, a, outs, out_type: int, ldc: int, col_offset: int, rows: int,
                            swiglu: bool = False, stream=None) -> None:
         """qlinear_run_device_scatter: the output columns go to column col_offset of every

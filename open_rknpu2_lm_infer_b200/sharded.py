@@ -14,6 +14,11 @@ single-GPU run.  Two ways to put the [M][N] output together on every rank:
   ``qlinear_peer_buffer_*``), then a one-warp kernel raises this rank's flag in every rank's
   signal array and waits for all of them (``qlinear_peer_signal_wait``), so the output is
   complete on every rank.  No gather, no assembly pass, no collective per call.
+  With ``multicast=True`` the exchange buffers are torch symmetric memory with an NVSwitch
+  multicast (NVLS) mapping: the tensor-core GEMM stores each element once through the
+  multicast address and the switch writes it into every rank's buffer
+  (``qlinear_run_device_multicast``), so a rank sends its columns over NVLink once instead
+  of once per peer.
 
 ``ShardedMLP`` splits a whole MLP block instead (gate/up columns and down rows together:
 no gather of the middle, an exact all-reduce of int32 partial accumulators).
@@ -55,7 +60,7 @@ class ShardedLinear:
     """One rank's shard of a column-parallel quantized linear."""
 
     def __init__(self, backend, matrix, group=None, fused_exchange: bool = False,
-                 max_rows: int = 0, out_dtype=None):
+                 max_rows: int = 0, out_dtype=None, multicast: bool = False):
         import torch.distributed as dist
         self.backend = backend
         self.group = group
@@ -68,7 +73,9 @@ class ShardedLinear:
         self.ns = hi - lo
         self.linear = backend.load_shard(matrix, lo, hi)
         self._bufs = {}
-        self._xbufs = {}  # output dtype -> (own ptr, peer ptrs, [max_rows][N] view, type code)
+        self.multicast = multicast
+        self._xbufs = {}  # output dtype -> exchange buffer record (own, peers, view, type, mc)
+        self._keep = []   # symmetric-memory tensors and handles of the multicast exchange
         self._default_dtype = None
         self._sig = None    # signal arrays in rank order (this rank's own at self.rank)
         self._epoch = 0
@@ -90,13 +97,17 @@ class ShardedLinear:
         if dtype in self._xbufs:
             raise ValueError(f"exchange buffer for {dtype} exists")
         elem, typestr = (2, "<f2") if dtype == torch.float16 else (4, "<f4")
+        if self.multicast:
+            self._add_multicast_exchange(max_rows, dtype)
+            return
         ptr, handle = self.backend.peer_buffer_create(max_rows * self.n * elem)
         handles = [None] * self.world
         dist.all_gather_object(handles, handle, group=self.group)
         peers = [self.backend.peer_buffer_open(h) for r, h in enumerate(handles) if r != self.rank]
         dev = torch.device("cuda", self.backend.device)
         view = torch.as_tensor(_DeviceArray(ptr, (max_rows, self.n), typestr), device=dev)
-        self._xbufs[dtype] = (ptr, peers, view, L.F16 if dtype == torch.float16 else L.F32)
+        self._xbufs[dtype] = {"own": ptr, "peers": peers, "view": view, "mc": 0,
+                              "type": L.F16 if dtype == torch.float16 else L.F32}
         if self._default_dtype is None:
             self._default_dtype = dtype
         if self._sig is None:
@@ -106,9 +117,50 @@ class ShardedLinear:
             self._sig = [sptr if r == self.rank else self.backend.peer_buffer_open(h)
                          for r, h in enumerate(shandles)]
 
+    def _add_multicast_exchange(self, max_rows: int, dtype) -> None:
+        """Collective: the [max_rows][N] exchange buffer and the signal array in torch
+        symmetric memory (every rank's copy mapped here, plus the NVSwitch multicast
+        address of the buffers)."""
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+        from . import _lib as L
+        group = self.group or dist.group.WORLD
+        if hasattr(symm_mem, "enable_symm_mem_for_group"):
+            symm_mem.enable_symm_mem_for_group(group.group_name)
+        dev = torch.device("cuda", self.backend.device)
+        buf = symm_mem.empty((max_rows, self.n), dtype=dtype, device=dev)
+        hdl = symm_mem.rendezvous(buf, group.group_name)
+        mc = int(hdl.multicast_ptr)
+        if not mc:
+            raise RuntimeError("multicast exchange: no NVSwitch multicast mapping on this node")
+        # the handle's addresses are those of the symmetric allocation holding the tensor;
+        # the tensor sits `off` bytes into it on every rank (and in the multicast mapping)
+        off = buf.data_ptr() - int(hdl.buffer_ptrs[self.rank])
+        if off < 0 or off != int(getattr(hdl, "offset", off)):
+            raise RuntimeError("multicast exchange: unexpected symmetric-memory layout")
+        ptrs = [int(p) + off for p in hdl.buffer_ptrs]
+        mc += off
+        self._keep += [buf, hdl]
+        self._xbufs[dtype] = {"own": ptrs[self.rank],
+                              "peers": [p for r, p in enumerate(ptrs) if r != self.rank],
+                              "view": buf, "mc": mc,
+                              "type": L.F16 if dtype == torch.float16 else L.F32}
+        if self._default_dtype is None:
+            self._default_dtype = dtype
+        if self._sig is None:
+            sig = symm_mem.empty((self.world,), dtype=torch.int64, device=dev)
+            sig.zero_()
+            hs = symm_mem.rendezvous(sig, group.group_name)
+            self._keep += [sig, hs]
+            soff = sig.data_ptr() - int(hs.buffer_ptrs[self.rank])
+            self._sig = [int(p) + soff for p in hs.buffer_ptrs]
+            torch.cuda.synchronize(dev)
+            dist.barrier(group=self.group)  # every rank's flags are zero before any signal
+
     @property
     def output(self):
-        return self._xbufs[self._default_dtype][2] if self._xbufs else None
+        return self._xbufs[self._default_dtype]["view"] if self._xbufs else None
 
     def run_exchange(self, a, rows: int, stream=None, out_dtype=None):
         """Fused split-N: this rank's columns go straight into every rank's exchange buffer of
@@ -119,11 +171,16 @@ class ShardedLinear:
         key = out_dtype or self._default_dtype
         if key not in self._xbufs:
             raise RuntimeError("no exchange buffer for this output type (add_exchange)")
-        own, peers, view, out_type = self._xbufs[key]
+        x = self._xbufs[key]
+        view = x["view"]
         if not 1 <= rows <= view.shape[0]:
             raise ValueError("rows out of range for the exchange buffer")
-        self.linear.run_device_scatter(a, [own] + peers, out_type, self.n, self.lo, rows,
-                                       stream=stream)
+        if x["mc"]:
+            self.linear.run_device_multicast(a, [x["own"]] + x["peers"], x["mc"], x["type"],
+                                             self.n, self.lo, rows, stream=stream)
+        else:
+            self.linear.run_device_scatter(a, [x["own"]] + x["peers"], x["type"], self.n,
+                                           self.lo, rows, stream=stream)
         self._epoch += 1
         self.backend.peer_signal_wait(self._sig, self.rank, self._epoch, stream=stream)
         return view[:rows]
@@ -132,17 +189,23 @@ class ShardedLinear:
         """Collective: every rank unmaps its peers' buffers, then frees its own."""
         import torch
         import torch.distributed as dist
-        if self._xbufs:
+        if self._xbufs and self.multicast:
             torch.cuda.synchronize(self.backend.device)  # no exchange kernel in flight
-            for own, peers, _, _ in self._xbufs.values():
-                for p in peers:
+            dist.barrier(group=self.group)  # no rank still reads or writes a peer's buffer
+            self._xbufs = {}
+            self._sig = None
+            self._keep = []
+        elif self._xbufs:
+            torch.cuda.synchronize(self.backend.device)  # no exchange kernel in flight
+            for x in self._xbufs.values():
+                for p in x["peers"]:
                     self.backend.peer_buffer_free(p, True)
             for r, p in enumerate(self._sig):
                 if r != self.rank:
                     self.backend.peer_buffer_free(p, True)
             dist.barrier(group=self.group)  # every peer unmapped this rank's buffers
-            for own, _, _, _ in self._xbufs.values():
-                self.backend.peer_buffer_free(own, False)
+            for x in self._xbufs.values():
+                self.backend.peer_buffer_free(x["own"], False)
             self.backend.peer_buffer_free(self._sig[self.rank], False)
             self._xbufs = {}
             self._sig = None

@@ -49,6 +49,19 @@ for bits, k, n, rows in [(4, 2560, 4096, 300), (8, 4096, 2048, 3), (4, 8192, 286
             torch.cuda.synchronize()
             assert torch.equal(got, want_t), (rank, "fused", dtype, bits, k, n, rows)
         fx.close()
+    # the exchange through NVSwitch multicast (torch symmetric memory, multimem stores)
+    try:
+        mx = ShardedLinear(b, qm, fused_exchange=True, max_rows=rows, multicast=True)
+    except RuntimeError as e:
+        print(f"rank {rank} multicast unavailable: {e}")
+        mx = None
+    if mx is not None:
+        for _ in range(2):
+            got = mx.run_exchange(x, rows)
+            torch.cuda.synchronize()
+            assert torch.equal(got, want), (rank, "multicast", bits, k, n, rows)
+        mx.close()
+        print(f"rank {rank} multicast ok {bits} {k} {n} {rows}")
     sh.linear.close(); full.close()
 # split-K MLP: gate/up columns and down rows split together, all-reduces of the row maxima
 # and the int32 partial accumulators; equal to the single-GPU block bit for bit
