@@ -72,6 +72,12 @@ constexpr int W4_MAX_TOK = 128;
 #define QL_W4_CONV_BATCH 1
 #endif
 constexpr int W4_CONV_BATCH = QL_W4_CONV_BATCH;  // stages a converter warp unpacks per wait
+#ifndef QL_W4_CONV_GROUPS
+#define QL_W4_CONV_GROUPS 1
+#endif
+// groups of 4 converter warps (one per tensor-memory lane quadrant); group g unpacks the
+// k-block iterations it with it % W4_CONV_GROUPS == g
+constexpr int W4_CONV_GROUPS = QL_W4_CONV_GROUPS;
 constexpr int EPI_WARPS = 8;
 constexpr int MAX_DYN_SMEM = 232448;        // 227 KB opt-in per block on sm_100
 constexpr int SMEM_RESERVE = 1024 + 1024;   // alignment slack + barriers
@@ -219,7 +225,7 @@ __device__ __forceinline__ void sk_split(const GemmArgs &p, int ncl, int t, int 
 }
 
 template <int BITS>
-constexpr int gemm_threads() { return (2 + EPI_WARPS + (BITS == 4 ? 4 : 0)) * 32; }
+constexpr int gemm_threads() { return (2 + EPI_WARPS + (BITS == 4 ? 4 * W4_CONV_GROUPS : 0)) * 32; }
 
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
@@ -740,7 +746,8 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
         // 8 * sum_k q[m][k].  Word i of a row's 16 covers k = 8i .. 8i + 7: its low nibbles
         // k 8i .. 8i + 3 (column 2i), its high nibbles 8i + 4 .. 8i + 7 (column 2i + 1).
         if constexpr (BITS == 4) {
-            const int ct = threadIdx.x - (2 + EPI_WARPS) * 32;  // 0..127
+            const int ct = threadIdx.x - (2 + EPI_WARPS) * 32;  // 0 .. 128 groups - 1
+            const int grp = ct >> 7;
             const int q = warp & 3;
             const int row = q * 32 + lane;
             const int swz = (row >> 1) & 3;
@@ -749,6 +756,7 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
             uint32_t as = 0, aph = 0;  // tensor-memory slot it is unpacked into
             Units cu(p, (int)cid, (int)ncl);
             bool okw = true;
+            uint32_t it = 0;
             while (cu.live && okw) {
                 // W4_CONV_BATCH stages per round: their tensor-memory writes complete under
                 // one tcgen05.wait::st before the stages are announced
@@ -756,6 +764,13 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                 int nb = 0;
 #pragma unroll
                 for (int b = 0; b < W4_CONV_BATCH; b++) {
+                    // the other groups' iterations
+                    while (W4_CONV_GROUPS > 1 && cu.live && (int)(it % W4_CONV_GROUPS) != grp) {
+                        if (++s == (uint32_t)S) { s = 0; ph ^= 1; }
+                        if (++as == (uint32_t)A_SLOTS) { as = 0; aph ^= 1; }
+                        cu.advance();
+                        it++;
+                    }
                     if (!cu.live) break;
                     // the MMA released the tensor-memory slot (iteration it - A_SLOTS) and this
                     // iteration's packed tile landed; the warp stays converged
@@ -781,15 +796,17 @@ __global__ void __launch_bounds__(gemm_threads<BITS>(), 1)
                     if (++s == (uint32_t)S) { s = 0; ph ^= 1; }
                     if (++as == (uint32_t)A_SLOTS) { as = 0; aph ^= 1; }
                     cu.advance();
+                    it++;
                 }
                 if (!okw) break;
+                if (nb == 0) break;
                 tmem_st_wait();
                 // the writes before the arrivals, ordered for the MMAs issued after the wait
                 tc_fence_before();
 #pragma unroll
                 for (int b = 0; b < W4_CONV_BATCH; b++)
                     if (b < nb) mbar_arrive(&cdone[bs[b]]);
-                if (ct == 0) {
+                if ((ct & 127) == 0) {
 #pragma unroll
                     for (int b = 0; b < W4_CONV_BATCH; b++) {
                         if (b >= nb || !okw) break;

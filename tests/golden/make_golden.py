@@ -133,9 +133,11 @@ def edge_cases():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("QLINEAR_REFERENCE_TREE",
-                                                           "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("QLINEAR_REFERENCE_TREE"),
+                    help="root of the reference tree (or set QLINEAR_REFERENCE_TREE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give the reference tree with --reference or QLINEAR_REFERENCE_TREE")
     quantize = load_reference_quantize(args.reference)
     out = {}
     total_disagree = 0
