@@ -3,19 +3,18 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload cfg4|cfg0|cfg1|cfg4_m8192]
-                    [--exchange auto|fused|multicast|gather] [--w4-packed-only]
+                    [--exchange fused|multicast|gather] [--w4-packed-only]
     python bench.py --sweep [--sweep-cases cfg0,cfg1,...]   # every named shape, one GPU
     python bench.py --mlp [--mlp-rows M] [--gpus N]           # the cfg2 MLP block
 
 Headline workload (default ``cfg4``): the W4A8 linear K=8192, N=28672 at M=512 tokens,
 split column-parallel over N GPUs (each rank owns N/g output channels); every rank ends
-with the whole fp16 [M][N] output.  The exchange: ``fused`` -- the GEMM's epilogues store
-each rank's columns into every rank's buffer over NVLink and a one-warp peer-flag kernel
-signals completion; ``multicast`` -- the same with one store per element through the
-NVSwitch multicast address of every rank's buffer; ``gather`` -- an NCCL all-gather of the
-slabs and the [g][M][N/g] -> [M][N] assembly; ``auto`` (default) -- multicast from
-MULTICAST_MIN_WORLD ranks on (falling back to fused where the node has no multicast),
-fused below.  A step is one pass of the path over one batch:
+with the whole fp16 [M][N] output.  The exchange: ``fused`` (default) -- the GEMM's
+epilogues store each rank's columns into every rank's buffer over NVLink and a one-warp
+peer-flag kernel signals completion; ``multicast`` -- the same with one store per element
+through the NVSwitch multicast address of every rank's buffer; ``gather`` -- an NCCL
+all-gather of the slabs and the [g][M][N/g] -> [M][N] assembly.  A step is one pass of the
+path over one batch:
 act-quant -> tcgen05 GEMM (-> exchange).  ``value`` is whole-job TOPS (2*M*K*N / step time,
 device-timed with CUDA events, max over ranks), inputs resident in HBM, L2 flushed between
 timed steps by a 256 MiB write outside the timed region.  Scaling is strong (the layer is
@@ -72,8 +71,7 @@ def parse():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg4")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="target CPU time of the oracle baseline sample")
-    ap.add_argument("--exchange", choices=["auto", "gather", "fused", "multicast"],
-                    default="auto",
+    ap.add_argument("--exchange", choices=["gather", "fused", "multicast"], default="fused",
                     help="split-N output exchange at N>1: NCCL all-gather + column assembly, "
                          "or the kernels' epilogues storing into every rank's buffer")
     ap.add_argument("--no-decode", action="store_true")
@@ -337,17 +335,8 @@ def run_ours(args, rank, world, local_rank):
         # of the slabs + column assembly, or (fused) by the kernels' epilogues storing each
         # rank's columns into every rank's buffer over NVLink
         from open_rknpu2_lm_infer_b200.sharded import ShardedLinear
-        try:
-            sharded = ShardedLinear(backend, qm, fused_exchange=fused, max_rows=m,
-                                    multicast=args.exchange == "multicast")
-        except RuntimeError as e:
-            # no NVSwitch multicast mapping on this node (the same answer on every rank):
-            # the peer-store exchange instead
-            if args.exchange != "multicast" or not args.exchange_auto:
-                raise
-            print(f"multicast exchange unavailable ({e}); peer stores instead", file=sys.stderr)
-            args.exchange = "fused"
-            sharded = ShardedLinear(backend, qm, fused_exchange=True, max_rows=m)
+        sharded = ShardedLinear(backend, qm, fused_exchange=fused, max_rows=m,
+                                multicast=args.exchange == "multicast")
         exchange_used = {"fused": "fused into the kernels, NVLink peer stores "
                                   "(qlinear_run_device_scatter)",
                          "multicast": "fused into the kernels, NVSwitch multicast stores "
@@ -985,17 +974,9 @@ def run_sweep(args):
     backend.close()
 
 
-# the split-N output exchange --exchange auto picks: NVSwitch multicast stores from this many
-# ranks on (each rank's NVLink egress is then its own columns once), peer stores below
-MULTICAST_MIN_WORLD = 4
-
-
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    args.exchange_auto = args.exchange == "auto"
-    if args.exchange_auto:
-        args.exchange = "multicast" if world >= MULTICAST_MIN_WORLD else "fused"
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.gpus != world and world > 1:

@@ -216,7 +216,7 @@ QLINEAR_API int qlinear_run_device_scatter(qlinear_backend *backend, const qline
  * own).  The tensor-core GEMM (rows above the decode path's 8) stores each output element
  * once through mc_dev and the switch writes it into every rank's buffer, so each GPU sends
  * its columns over NVLink once instead of once per peer; the decode GEMV stores to c_devs[]
- * as qlinear_run_device_scatter does.  fp16 output: col_offset and ldc must be even
+ * as qlinear_run_device_scatter does.  fp16 output: col_offset, ldc and N must be even
  * (multimem stores are 32 bits wide).  The kernels end with a system-scope fence, as for
  * qlinear_run_device_scatter. */
 QLINEAR_API int qlinear_run_device_multicast(qlinear_backend *backend,

@@ -697,7 +697,7 @@ int qlinear_run_device_multicast(qlinear_backend *b, const qlinear_weights *w, c
     if (!b || !w || w->backend != b || !c_devs || !mc_dev || ndev < 1 || ndev > kMaxOutputs ||
         col_offset < 0 || ldc < col_offset + w->view.N)
         return QLINEAR_ERR_PARAM;
-    if (c_type == QLINEAR_F16 && ((col_offset | ldc) & 1)) return QLINEAR_ERR_PARAM;
+    if (c_type == QLINEAR_F16 && ((col_offset | ldc | w->view.N) & 1)) return QLINEAR_ERR_PARAM;
     OutputSet o{};
     for (int d = 0; d < ndev; d++) o.dst[d] = c_devs[d];
     o.count = ndev;
