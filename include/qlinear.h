@@ -151,7 +151,9 @@ QLINEAR_API int qlinear_backend_prepare(qlinear_backend *backend, int rows);
 
 /* Replaces rk_npu_w4a8_run_f32 (src/npu.rs:1047) and rk_npu_f32i8f32_run_dynamic
  * (src/npu.rs:1054): a_host f32 [rows][K] -> c_host f32 [rows][N], synchronous.
- * Unlike the reference (rows <= 256, src/npu.rs:152-156) any rows >= 1 is accepted. */
+ * Unlike the reference (rows <= 256, src/npu.rs:152-156) any rows >= 1 is accepted.
+ * Host buffers in ordinary (pageable) memory go through the backend's pinned staging;
+ * page-locked buffers (cudaHostAlloc / cudaHostRegister) are copied by DMA directly. */
 QLINEAR_API int qlinear_run_f32(qlinear_backend *backend, const qlinear_weights *weights, const float *a_host,
                     float *c_host, int rows);
 /* Replaces rk_npu_w4a8_run_swiglu_f32 (src/npu.rs:1045): c_host f32 [rows][N/2] with

@@ -765,6 +765,20 @@ int qlinear_peer_buffer_free(qlinear_backend *b, void *dev_ptr, int opened) {
     return QLINEAR_OK;
 }
 
+// Whether [p, p + bytes) is page-locked host memory the GPU can copy from or to directly
+// (cudaHostAlloc'd or cudaHostRegister'ed): both ends are checked.
+static bool host_pinned(const void *p, size_t bytes) {
+    for (const char *q : {static_cast<const char *>(p), static_cast<const char *>(p) + bytes - 1}) {
+        cudaPointerAttributes at{};
+        if (cudaPointerGetAttributes(&at, q) != cudaSuccess) {
+            cudaGetLastError();  // not a CUDA pointer: clear the error, use the staging path
+            return false;
+        }
+        if (at.type != cudaMemoryTypeHost) return false;
+    }
+    return true;
+}
+
 static int run_host(qlinear_backend *b, const qlinear_weights *w, const float *a_host,
                     float *c_host, long long ldc, int rows, unsigned flags) {
     if (!b || !w || w->backend != b || !a_host || !c_host || rows < 1) return QLINEAR_ERR_PARAM;
@@ -778,6 +792,32 @@ static int run_host(qlinear_backend *b, const qlinear_weights *w, const float *a
     const size_t in_bytes = (size_t)rows * v.K * sizeof(float);
     const size_t out_bytes = (size_t)rows * width * sizeof(float);
     int st;
+    // Caller buffers in page-locked memory: copied by DMA directly, no staging and no host
+    // copies (the input [rows][K] in one transfer, the output rows of stride ldc in one
+    // 2-D transfer).
+    if (host_pinned(a_host, in_bytes) &&
+        host_pinned(c_host, ((size_t)(rows - 1) * ldc + width) * sizeof(float))) {
+        if ((st = ensure_dev(&b->d_in, &b->d_in_bytes, in_bytes)) ||
+            (st = ensure_dev(&b->d_out, &b->d_out_bytes, out_bytes)))
+            return st;
+        QL_TRY(cudaMemcpyAsync(b->d_in, a_host, in_bytes, cudaMemcpyHostToDevice, b->stream));
+        st = run_device_impl(b, w, b->d_in, QLINEAR_F32, single_output(b->d_out), QLINEAR_F32,
+                             width, rows, flags, b->stream);
+        if (st) return st;
+        QL_TRY(cudaMemcpy2DAsync(c_host, (size_t)ldc * sizeof(float), b->d_out,
+                                 (size_t)width * sizeof(float), (size_t)width * sizeof(float),
+                                 rows, cudaMemcpyDeviceToHost, b->stream));
+        QL_TRY(cudaMemcpyAsync(b->h_err, b->d_err, sizeof(unsigned), cudaMemcpyDeviceToHost,
+                               b->stream));
+        QL_TRY(cudaStreamSynchronize(b->stream));
+        if (*b->h_err) {
+            cudaMemsetAsync(b->d_err, 0, sizeof(unsigned), b->stream);
+            cudaStreamSynchronize(b->stream);
+            reset_after_timeout(b);
+            return QLINEAR_ERR_TIMEOUT;
+        }
+        return QLINEAR_OK;
+    }
     if ((st = ensure_host(&b->h_in, &b->h_in_bytes, in_bytes)) ||
         (st = ensure_host(&b->h_out, &b->h_out_bytes, out_bytes)) ||
         (st = ensure_dev(&b->d_in, &b->d_in_bytes, in_bytes)) ||
