@@ -42,6 +42,7 @@ struct qlinear_backend {
     int num_sms = 148;
     int gemm_pairs[2] = {0, 0};  // resident CTA pairs of the W4 / W8 GEMM
     cudaStream_t stream = nullptr;  // host-path calls and uploads
+    cudaStream_t stream_in = nullptr;  // host path, page-locked input: row pieces sent ahead
     unsigned *d_err = nullptr;
     unsigned *h_err = nullptr;      // pinned
     // activation workspace
@@ -584,6 +585,7 @@ void destroy_backend(qlinear_backend *b) {
     b->pool.reset();
     for (auto &e : b->prof_events)
         for (auto x : e) cudaEventDestroy(x);
+    if (b->stream_in) cudaStreamDestroy(b->stream_in);
     if (b->stream) cudaStreamDestroy(b->stream);
     delete b;
 }
@@ -793,20 +795,48 @@ static int run_host(qlinear_backend *b, const qlinear_weights *w, const float *a
     const size_t out_bytes = (size_t)rows * width * sizeof(float);
     int st;
     // Caller buffers in page-locked memory: copied by DMA directly, no staging and no host
-    // copies (the input [rows][K] in one transfer, the output rows of stride ldc in one
-    // 2-D transfer).
+    // copies.  Large calls go in pieces of 128 rows: the input pieces are sent on a second
+    // stream, and each piece is computed and its output rows (stride ldc, one 2-D transfer)
+    // sent back as soon as its input has landed, so the output of one piece travels back
+    // while the next piece's input travels in (the link is full duplex).
     if (host_pinned(a_host, in_bytes) &&
         host_pinned(c_host, ((size_t)(rows - 1) * ldc + width) * sizeof(float))) {
         if ((st = ensure_dev(&b->d_in, &b->d_in_bytes, in_bytes)) ||
             (st = ensure_dev(&b->d_out, &b->d_out_bytes, out_bytes)))
             return st;
-        QL_TRY(cudaMemcpyAsync(b->d_in, a_host, in_bytes, cudaMemcpyHostToDevice, b->stream));
-        st = run_device_impl(b, w, b->d_in, QLINEAR_F32, single_output(b->d_out), QLINEAR_F32,
-                             width, rows, flags, b->stream);
-        if (st) return st;
-        QL_TRY(cudaMemcpy2DAsync(c_host, (size_t)ldc * sizeof(float), b->d_out,
-                                 (size_t)width * sizeof(float), (size_t)width * sizeof(float),
-                                 rows, cudaMemcpyDeviceToHost, b->stream));
+        if (!b->stream_in)
+            QL_TRY(cudaStreamCreateWithFlags(&b->stream_in, cudaStreamNonBlocking));
+        const int piece = rows >= 256 ? 128 : rows;
+        const int npieces = (rows + piece - 1) / piece;
+        while ((int)b->chunk_events.size() < npieces) {
+            cudaEvent_t e;
+            QL_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+            b->chunk_events.push_back(e);
+        }
+        const char *a_bytes = reinterpret_cast<const char *>(a_host);
+        char *d_in = static_cast<char *>(b->d_in);
+        const size_t in_row = (size_t)v.K * sizeof(float), out_row = (size_t)width * sizeof(float);
+        for (int i = 0; i < npieces; i++) {
+            const int r0 = i * piece, n = std::min(piece, rows - r0);
+            QL_TRY(cudaMemcpyAsync(d_in + r0 * in_row, a_bytes + r0 * in_row, n * in_row,
+                                   cudaMemcpyHostToDevice, b->stream_in));
+            QL_TRY(cudaEventRecord(b->chunk_events[i], b->stream_in));
+        }
+        char *d_out = static_cast<char *>(b->d_out);
+        for (int i = 0; i < npieces; i++) {
+            const int r0 = i * piece, n = std::min(piece, rows - r0);
+            QL_TRY(cudaStreamWaitEvent(b->stream, b->chunk_events[i], 0));
+            st = run_device_impl(b, w, d_in + r0 * in_row, QLINEAR_F32,
+                                 single_output(d_out + r0 * out_row), QLINEAR_F32, width, n,
+                                 flags, b->stream);
+            if (st) {
+                cudaStreamSynchronize(b->stream_in);
+                return st;
+            }
+            QL_TRY(cudaMemcpy2DAsync(c_host + (size_t)r0 * ldc, (size_t)ldc * sizeof(float),
+                                     d_out + r0 * out_row, out_row, out_row, n,
+                                     cudaMemcpyDeviceToHost, b->stream));
+        }
         QL_TRY(cudaMemcpyAsync(b->h_err, b->d_err, sizeof(unsigned), cudaMemcpyDeviceToHost,
                                b->stream));
         QL_TRY(cudaStreamSynchronize(b->stream));
