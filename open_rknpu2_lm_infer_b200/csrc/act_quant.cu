@@ -13,6 +13,9 @@
 // k-block, the pad zeroed), the f32 scale per row and the i32 sum of the row's codes
 // (used by the W4 epilogue, whose weights are stored offset by +8).
 //
+// Launched with programmatic stream serialization and a griddepcontrol.wait before any memory
+// access, so its launch overlaps the tail of the preceding kernel (measured on B200: cfg0
+// 26.8 -> 24.5 us per act-quant + GEMM call, the 36-layer prefill pass 4995 -> 4743 us).
 // One CTA per row; the row is read once with 16-byte loads and held in registers (up to
 // kCache chunks per thread; longer rows are re-read from L1/L2), the max is reduced with
 // warp shuffles (max is order independent, so the result is exact), codes are written
@@ -96,6 +99,9 @@ __global__ void __launch_bounds__(kThreads) act_quant_vec_kernel(
     const T *__restrict__ x, long long ldx, int K, int Kp, int round_mode,
     int8_t *__restrict__ codes, float *__restrict__ scales, int32_t *__restrict__ rowsums,
     const float *__restrict__ amax_in, int early) {
+    // launched with programmatic stream serialization: nothing is read or written before
+    // the preceding kernel has completed
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if (early) asm volatile("griddepcontrol.launch_dependents;");
     constexpr int V = Vec<T>::N;
     __shared__ float redf[32];
@@ -180,6 +186,7 @@ __global__ void __launch_bounds__(kThreads) act_quant_scalar_kernel(
     const T *__restrict__ x, long long ldx, int K, int Kp, int round_mode,
     int8_t *__restrict__ codes, float *__restrict__ scales, int32_t *__restrict__ rowsums,
     const float *__restrict__ amax_in, int early) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if (early) asm volatile("griddepcontrol.launch_dependents;");
     __shared__ float redf[32];
     __shared__ int redi[32];
@@ -226,6 +233,23 @@ int resident_ctas(K kern, int (&cache)[64]) {
     return cache[dev] > 0 ? cache[dev] : 0;
 }
 
+// A launch with programmatic stream serialization (the kernel waits with griddepcontrol.wait
+// before it touches memory): its launch overlaps the tail of the preceding kernel.
+template <typename Kern, typename... Args>
+cudaError_t launch_pdl(Kern kern, int rows, cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(rows);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 template <typename T>
 cudaError_t launch_typed(const T *x, long long ldx, int rows, int K, int Kp, int round_mode,
                          int8_t *codes, float *scales, int32_t *rowsums, cudaStream_t stream,
@@ -238,13 +262,12 @@ cudaError_t launch_typed(const T *x, long long ldx, int rows, int K, int Kp, int
     static int cap_vec[64] = {0}, cap_scalar[64] = {0};
     if (vec) {
         const int early = rows <= resident_ctas(act_quant_vec_kernel<T>, cap_vec) ? 1 : 0;
-        act_quant_vec_kernel<T><<<rows, kThreads, 0, stream>>>(x, ldx, K, Kp, round_mode, codes,
-                                                               scales, rowsums, amax_in, early);
+        return launch_pdl(act_quant_vec_kernel<T>, rows, stream, x, ldx, K, Kp, round_mode,
+                          codes, scales, rowsums, amax_in, early);
     } else {
         const int early = rows <= resident_ctas(act_quant_scalar_kernel<T>, cap_scalar) ? 1 : 0;
-        act_quant_scalar_kernel<T><<<rows, kThreads, 0, stream>>>(x, ldx, K, Kp, round_mode,
-                                                                  codes, scales, rowsums, amax_in,
-                                                                  early);
+        return launch_pdl(act_quant_scalar_kernel<T>, rows, stream, x, ldx, K, Kp, round_mode,
+                          codes, scales, rowsums, amax_in, early);
     }
     return cudaGetLastError();
 }
