@@ -8,8 +8,9 @@
 // y = (f32(acc) * s_a[m]) * s_w[n] (src/npu.rs:1117), written as f32 / fp16 / raw i32;
 // with swiglu, out[m][j] = silu(y[m][j]) * y[m][N/2 + j] (src/npu.rs:1202-1208).
 //
-// Work split: CTA c (one per SM, 16 warps) owns the contiguous output rows [r0, r1); warp w
-// owns the CTA's rows w, w + 16, ...  A task is one chunk of one row (with swiglu: the gate
+// Work split: CTA c (one per SM, 16 warps) owns the contiguous output rows [r0, r1) (an even
+// split, or for small layers a ramp from more rows at the first CTA to fewer at the last:
+// gemv_row_start); warp w owns the CTA's rows w, w + 16, ...  A task is one chunk of one row (with swiglu: the gate
 // row n and its up row N/2 + n together): U 16-byte units per lane, i.e. 512*U contiguous
 // bytes per segment, read with ld.global.nc.L1::no_allocate straight into registers.  A warp
 // keeps D tasks in flight in a register ring (D*U*16 bytes per lane, about 192 KB per SM in
@@ -147,6 +148,7 @@ struct GemvArgs {
     const uint8_t *wq;
     const float *wscale;
     int N, Kp, K;
+    int skew_q10;      // 0: rows_per_cta rows per CTA; else the ramp gemv_row_start draws
     const void *xin;
     int in_type;
     long long ldx;
@@ -157,10 +159,29 @@ struct GemvArgs {
     void *out;  // the output when one buffer takes it; several: the kernel's OutputSet
     int out_type;
     long long ldc;
-    int rows_per_cta;  // output rows (channels, or gate rows with swiglu) per CTA
+    int rows_per_cta;  // output rows (channels, or gate rows with swiglu) per CTA (the most)
     int nch;           // chunks per row
     unsigned *err;
 };
+// 128 bytes: one more field past that (the skew once sat there) measured the W4 layer at
+// eight rows 52.3 -> 57.5 us per call, so new fields go into the padding above
+static_assert(sizeof(GemvArgs) == 128, "GemvArgs grew past 128 bytes");
+
+// Skewed row split (single-output kernel, one or two activation rows): CTA j of G owns rows
+// [R(j), R(j+1)) with R(j) = n ((1 + s) j G - s j^2) / G^2, s = q / 1024 -- a linear ramp from
+// (1 + s) n / G rows at the first CTA to (1 - s) n / G at the last.  Why: with the early
+// dependent launch, call i+1's CTAs take the SMs in blockIdx order as call i's CTAs exit, so
+// its last CTAs land when call i completes and, with an even split, then stream a whole
+// share; the ramp gives the early CTAs (which stream while call i drains) more rows and the
+// late ones fewer.  Sized in bytes, not as a fraction: about 68 KB above and below the mean
+// share, so large layers (the lm_head: 2.6 MB per CTA) stay nearly even (a fixed 20-40% ramp
+// slowed the lm_head and the 117 MB W4 layer by 13-28%).  Measured on B200, same box,
+// alternating runs: cfg2's block at M=1 21.9 -> 19.6 us, the 36-layer decode pass 1157 ->
+// 1100 us per token (1118 -> 1072 us replayed as a CUDA graph), cfg1 W8 M=1 7.9 -> 7.8 us,
+// cfg4 W4 M=1 27.9 -> 27.6 us, the lm_head unchanged.
+__host__ __device__ inline int gemv_row_start(long long j, long long G, long long n, int q) {
+    return (int)(n * ((1024 + q) * j * G - q * j * j) / (1024 * G * G));
+}
 
 // Quantise the call's rows into xs (codes [MT][Kp], zero beyond M and K) and set s_scale /
 // s_rowsum.  TIn: __half or float; K and ldx are multiples of 16 / sizeof(TIn) and the rows
@@ -302,8 +323,15 @@ __device__ __forceinline__ void gemv_body(const GemvArgs &p,
     const int row_bytes = BITS == 8 ? p.Kp : p.Kp / 2;
     const int upr = row_bytes / 16;  // 16-byte units per row
     const int nrows_out = SWIGLU ? p.N / 2 : p.N;
-    const int r0 = blockIdx.x * p.rows_per_cta;
-    const int nr = max(0, min(nrows_out, r0 + p.rows_per_cta) - r0);
+    // plan() skews only at one or two rows; the clamp never bites (rows_per_cta is sized
+    // for the ramp)
+    constexpr bool SKEW = MT <= 2;
+    const bool skew = SKEW && p.skew_q10 != 0;
+    const int r0 = skew ? gemv_row_start(blockIdx.x, gridDim.x, nrows_out, p.skew_q10)
+                        : blockIdx.x * p.rows_per_cta;
+    const int nr = skew ? min(gemv_row_start(blockIdx.x + 1, gridDim.x, nrows_out, p.skew_q10) - r0,
+                              p.rows_per_cta)
+                        : max(0, min(nrows_out, r0 + p.rows_per_cta) - r0);
     // PAIR: the CTA's rows in two halves, [0, h1) and [h1, nr); a task covers local row lr
     // of both (the second half may be one row shorter)
     const int h1 = PAIR ? (nr + 1) / 2 : nr;
@@ -540,7 +568,22 @@ struct Plan {
     int rows_per_cta, grid, nch, units;
     size_t smem;
     bool bal;  // balanced (row, chunk) tasks; units then 1, 2 or 4
+    int skew_q10;  // skewed row split (gemv_row_start), 0: even
 };
+
+// The ramp of the skewed row split for a layer of `nrows` rows of `row_bytes` (x2 with
+// SwiGLU: gate and up rows) over `grid` CTAs at `mt` activation rows: q / 1024 = about 68 KB
+// over the mean bytes per CTA, at most 0.4, none below 1/64 or at four or more rows (there
+// the dot products take longer per byte and the ramp measured no gain: cfg1 at M=4 10.3 ->
+// 10.4 us with a 20% ramp, the W4 layer at M=8 slower).
+inline int gemv_skew_q10(long long nrows, long long row_bytes, int nseg, int grid, int mt) {
+    if (mt > 2 || grid < 2) return 0;
+    const long long ramp = 68 * 1024;
+    const long long cta_bytes = nrows * row_bytes * nseg / grid;
+    if (cta_bytes <= 0) return 0;
+    const long long q = std::min<long long>(410, ramp * 1024 / cta_bytes);
+    return q >= 16 ? (int)q : 0;
+}
 
 // Rows per CTA (one CTA per SM), chunks per row and units per lane, shared memory.
 // allow_bal: the caller launches the single-output kernel (the balanced mode is built only
@@ -563,7 +606,27 @@ inline bool plan(int rows, int Kp, int N, int bits, bool swiglu, int num_sms, Pl
     pl->units = round_units((lane_units + nch - 1) / nch);
     pl->smem = smem;
     pl->bal = false;
+    pl->skew_q10 = 0;
+    const int row_bytes = bits == 8 ? Kp : Kp / 2;
+    if (allow_bal) {
+        // the skewed split where it fits the shared-memory budget (else the even one, so a
+        // request that fits the even split never fails here)
+        const int g = std::min(num_sms, nrows);
+        const int q = gemv_skew_q10(nrows, row_bytes, swiglu ? 2 : 1, g, mt_of(rows));
+        if (q) {
+            const int pmax = (int)(((long long)nrows * (1024 + q) + 1024LL * g - 1) / (1024LL * g)) + 2;
+            const size_t smem_s = (size_t)mt_of(rows) * Kp + (size_t)(swiglu ? 2 : 1) * pmax * 4;
+            if (smem_s <= (size_t)kSmemBudget) {
+                pl->rows_per_cta = pmax;
+                pl->grid = g;
+                pl->smem = smem_s;
+                pl->skew_q10 = q;
+            }
+        }
+    }
     if (allow_bal && mt_of(rows) <= 2) {
+        const int per = pl->rows_per_cta;  // the busiest CTA's rows
+        const size_t smem = pl->smem;
         // time ~ the busiest warp's units per lane: whole rows, ceil(per / 16) rows of nch
         // chunks of `units`; balanced, ceil(per * nchb / 16) tasks of u units
         const long long whole = (long long)((per + kWarps - 1) / kWarps) * nch * pl->units;
@@ -616,6 +679,7 @@ cudaError_t launch_t(const WeightView &w, const GemvInput &in, int rows, const O
     a.ldc = ldc;
     a.rows_per_cta = pl.rows_per_cta;
     a.nch = pl.nch;
+    a.skew_q10 = pl.skew_q10;
     a.err = in.err;
     auto kern = gemv_kernel<BITS, MT, SWIGLU, U, SCATTER, BAL>;
     static int configured[64] = {0};  // per device: raise the opt-in limit once

@@ -280,3 +280,47 @@ def test_token_tile_and_tail_split_cover_every_token_once():
         assert (cover == 1).all(), (rows, np_, maxp)
         hit[split > 1] = True
     assert hit.get(True) and hit.get(False)
+
+
+# The decode GEMV's skewed row split (csrc/gemv_impl.cuh: gemv_row_start, gemv_skew_q10 and
+# the rows_per_cta bound plan() sizes the shared memory for), restated in exact integers.
+def _skew_q10(nrows, row_bytes, nseg, grid, mt):
+    if mt > 2 or grid < 2:
+        return 0
+    ramp = 68 * 1024
+    cta_bytes = nrows * row_bytes * nseg // grid
+    if cta_bytes <= 0:
+        return 0
+    q = min(410, ramp * 1024 // cta_bytes)
+    return q if q >= 16 else 0
+
+
+def _row_start(j, G, n, q):
+    return n * ((1024 + q) * j * G - q * j * j) // (1024 * G * G)
+
+
+@pytest.mark.parametrize("nrows,row_bytes,nseg,mt", [
+    (9728, 2560, 1, 1), (9728, 2560, 1, 2), (6144, 1280, 1, 1), (2560, 4096, 1, 1),
+    (9728, 1280, 2, 1), (2560, 9728, 1, 2), (28672, 4096, 1, 1), (151936, 2560, 1, 1),
+    (200, 512, 1, 1), (149, 128, 1, 1), (148, 128, 2, 2), (5000, 64, 1, 1)])
+@pytest.mark.parametrize("sms", [148, 132, 7])
+def test_gemv_skewed_rows_cover_every_row_once(nrows, row_bytes, nseg, mt, sms):
+    g = min(sms, nrows)
+    q = _skew_q10(nrows, row_bytes, nseg, g, mt)
+    if not q:
+        return
+    pmax = (nrows * (1024 + q) + 1024 * g - 1) // (1024 * g) + 2
+    starts = [_row_start(j, g, nrows, q) for j in range(g + 1)]
+    assert starts[0] == 0 and starts[-1] == nrows
+    counts = np.diff(starts)
+    assert counts.min() >= 0 and counts.max() <= pmax  # the kernel's clamp never bites
+    # a ramp: non-increasing up to the rounding of one row
+    assert np.all(np.diff(counts) <= 1)
+    # the int64 products of the kernel's formula stay far below 2^63
+    assert nrows * (1024 + q) * g * g < 2 ** 62
+
+
+def test_gemv_skew_only_at_one_or_two_rows():
+    assert _skew_q10(9728, 2560, 1, 148, 4) == 0 and _skew_q10(9728, 2560, 1, 148, 8) == 0
+    assert _skew_q10(9728, 2560, 1, 148, 1) == 410
+    assert _skew_q10(151936, 2560, 1, 148, 1) == 27  # the lm_head: a 2.6% ramp
